@@ -1,0 +1,125 @@
+"""ctypes binding of libfast_trimul_b200.so (the C ABI in include/fast_trimul_b200.h).
+
+The library is built in-tree (`python fast_trimul_b200/csrc/build.py`). Loading is
+lazy; `load()` raises `NativeLibraryMissing` when the .so is absent or lacks a
+symbol, and the CUDA backend lets that error propagate instead of silently
+falling back.
+"""
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfast_trimul_b200.so")
+
+# status codes (ftm_status)
+OK, BAD_SHAPE, BAD_DTYPE, BAD_ALIGN, UNSUPPORTED_ARCH, LAUNCH_FAILED, TIMEOUT, BAD_WORKSPACE, \
+    BAD_ARGUMENT = range(9)
+# dtypes (ftm_dtype) and modes (ftm_mode)
+F32, F16, BF16 = 0, 1, 2
+OUTGOING, INCOMING = 0, 1
+
+# every symbol the header declares, with (restype, argtypes)
+_vp, _i32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+
+
+class Problem(ctypes.Structure):
+    """Mirror of ftm_problem."""
+    _fields_ = [("batch", _i32), ("rows", _i32), ("cols", _i32), ("c_z", _i32), ("c_h", _i32),
+                ("mode", _i32), ("residual", _i32), ("z_dtype", _i32), ("out_dtype", _i32),
+                ("eps_in", ctypes.c_float), ("eps_out", ctypes.c_float)]
+
+
+_PP = ctypes.POINTER(Problem)
+_IP = ctypes.POINTER(ctypes.c_int)
+
+SIGNATURES = {
+    "ftm_packed_params_bytes": (_sz, [_i32, _i32]),
+    "ftm_pack_params": (ctypes.c_int, [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp, _vp]),
+    "ftm_workspace_bytes": (_sz, [_PP]),
+    "ftm_trimul_fwd": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ftm_input_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_contraction": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "ftm_output_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_check_error": (ctypes.c_int, [_vp, _IP, _vp]),
+    "ftm_workspace_error_word": (_vp, [_PP, _vp]),
+    "ftm_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "ftm_device_supported": (ctypes.c_int, [ctypes.c_int]),
+    "ftm_last_launch_count": (ctypes.c_int, []),
+}
+
+
+class NativeLibraryMissing(RuntimeError):
+    """The CUDA library is not built / not loadable: a hard error, never a fallback."""
+
+
+class NativeKernelError(RuntimeError):
+    """A launch failed or a device-side bounded wait expired."""
+
+
+class NativeDeclined(RuntimeError):
+    """The kernels do not support this input (shape / dtype / device); callers may
+    route it to another backend, exactly as the reference's guard does."""
+
+
+_lock = threading.Lock()
+_lib = None
+
+# counters the tests use to prove the native path ran
+stats = {"calls": 0, "kernel_launches": 0}
+
+
+def load():
+    """Load the shared library (once) and bind every declared symbol."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise NativeLibraryMissing(
+                f"{LIB_PATH} not found: build it with `python fast_trimul_b200/csrc/build.py`")
+        try:
+            lib = ctypes.CDLL(LIB_PATH)
+        except OSError as e:
+            raise NativeLibraryMissing(f"cannot load {LIB_PATH}: {e}") from e
+        for name, (res, args) in SIGNATURES.items():
+            try:
+                fn = getattr(lib, name)
+            except AttributeError as e:
+                raise NativeLibraryMissing(f"{LIB_PATH} lacks symbol {name}") from e
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def available():
+    try:
+        load()
+        return True
+    except NativeLibraryMissing:
+        return False
+
+
+def status_string(code):
+    return load().ftm_status_string(int(code)).decode()
+
+
+def check(code, what):
+    """Map an ftm_status to the exception the dispatcher understands."""
+    if code == OK:
+        return
+    msg = f"{what}: {status_string(code)} (status {code})"
+    if code in (BAD_SHAPE, BAD_DTYPE, BAD_ALIGN, UNSUPPORTED_ARCH):
+        raise NativeDeclined(msg)
+    raise NativeKernelError(msg)
+
+
+def record_launches():
+    n = load().ftm_last_launch_count()
+    stats["calls"] += 1
+    stats["kernel_launches"] += n
+    return n

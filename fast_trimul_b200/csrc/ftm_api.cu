@@ -1,0 +1,361 @@
+// C ABI of fast_trimul_b200 (declared in include/fast_trimul_b200.h): argument
+// checks, TMA tensor-map construction and the launch sequence of the three stages.
+#include <mutex>
+
+#include "../../include/fast_trimul_b200.h"
+#include "ftm_kernels.h"
+
+using namespace ftm;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+thread_local int g_last_launches = 0;
+
+int sm_count(int dev) {
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+bool arch_ok(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (dev_out) *dev_out = dev;
+  return ftm_device_supported(dev) == 1;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 128B-swizzled tiled map over `rank` dims; strides in bytes for dims 1..rank-1
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base,
+              const uint64_t* dims, const uint64_t* strides, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) s[i] = strides[i];
+  const CUresult r =
+      fn(m, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+CUtensorMapDataType tma_dtype(int dt) {
+  return dt == FTM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+int check_problem(const ftm_problem* p) {
+  if (!p) return FTM_BAD_ARGUMENT;
+  if (p->c_z != kC || p->c_h != kC) return FTM_BAD_SHAPE;
+  if (p->batch < 1 || p->rows < 1 || p->cols < 1) return FTM_BAD_SHAPE;
+  if (p->cols % 8 != 0) return FTM_BAD_SHAPE;  // TMA row strides must be 16-byte multiples
+  if (p->mode != FTM_OUTGOING && p->mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
+  if (p->mode == FTM_INCOMING && p->rows != p->cols) return FTM_BAD_SHAPE;
+  if (p->z_dtype != FTM_F16 && p->z_dtype != FTM_BF16) return FTM_BAD_DTYPE;
+  if (p->out_dtype != FTM_F16 && p->out_dtype != FTM_BF16 && p->out_dtype != FTM_F32)
+    return FTM_BAD_DTYPE;
+  const double elems = double(p->batch) * p->rows * p->cols * kC;
+  if (elems > 4.0e12) return FTM_BAD_SHAPE;
+  return FTM_OK;
+}
+
+// z as (C, S, R, B) [natural] or (C, R, S, B) [incoming: consecutive tile rows walk r]
+bool make_z_map(CUtensorMap* m, const ftm_problem* p, const void* z, bool transposed,
+                const PosTiling& tl) {
+  const uint64_t e = 2, C = kC, R = p->rows, S = p->cols, B = p->batch;
+  uint64_t dims[4], strides[3];
+  dims[0] = C;
+  if (!transposed) {
+    dims[1] = S; strides[0] = C * e;
+    dims[2] = R; strides[1] = S * C * e;
+  } else {
+    dims[1] = R; strides[0] = S * C * e;
+    dims[2] = S; strides[1] = C * e;
+  }
+  dims[3] = B;
+  strides[2] = R * S * C * e;
+  const uint32_t box[4] = {64, static_cast<uint32_t>(tl.vt), static_cast<uint32_t>(tl.ut), 1};
+  return make_map(m, tma_dtype(p->z_dtype), 4, z, dims, strides, box);
+}
+
+int stage_in(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+             void* a_cm, void* b_cm, int* err, cudaStream_t stream, int dev) {
+  PosTiling tl;
+  tl.init(p->batch, p->rows, p->cols);
+  const bool incoming = p->mode == FTM_INCOMING;
+  CUtensorMap zmap, wmap;
+  if (!make_z_map(&zmap, p, z, incoming, tl)) return FTM_LAUNCH_FAILED;
+  const PackedLayout L = PackedLayout::make(kC, kC);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  {
+    const uint64_t dims[2] = {kC, 4 * kC}, strides[1] = {kC * 2};
+    const uint32_t box[2] = {64, 256};
+    if (!make_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pk + L.w_in, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  const int grid = tl.tiles < sm_count(dev) ? tl.tiles : sm_count(dev);
+  cudaError_t e = launch_input_stage(
+      zmap, wmap, mask, reinterpret_cast<const float*>(pk + L.u_in),
+      reinterpret_cast<const float*>(pk + L.v_in), static_cast<__half*>(a_cm),
+      static_cast<__half*>(b_cm), tl, incoming ? 1 : 0, p->z_dtype == FTM_BF16 ? 1 : 0,
+      p->eps_in, err, grid, stream);
+  return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
+}
+
+int stage_contract(const void* A, const void* B, void* X, int L, int m, int k, int rpb, int blocks,
+                   int* err, cudaStream_t stream, int dev) {
+  CUtensorMap amap, bmap;
+  {
+    const uint64_t dims[3] = {uint64_t(k), uint64_t(m), uint64_t(L)};
+    const uint64_t strides[2] = {uint64_t(k) * 2, uint64_t(m) * k * 2};
+    const uint32_t box[3] = {kCtBK, kCtBM, 1};
+    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, A, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  {
+    const uint64_t dims[4] = {uint64_t(k), uint64_t(rpb), uint64_t(L), uint64_t(blocks)};
+    const uint64_t strides[3] = {uint64_t(k) * 2, uint64_t(rpb) * k * 2,
+                                 uint64_t(L) * rpb * k * 2};
+    const uint32_t box[4] = {kCtBK, kCtBN, 1, 1};
+    if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, B, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  const int n = rpb * blocks;
+  const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
+  const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
+  cudaError_t e = launch_contraction(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err,
+                                     grid, stream);
+  return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
+}
+
+int stage_out(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
+              const void* packed, void* out, int* err, cudaStream_t stream, int dev) {
+  PosTiling tl;
+  tl.init(p->batch, p->rows, p->cols);
+  CUtensorMap zmap, xmap, wmap;
+  if (!make_z_map(&zmap, p, z, false, tl)) return FTM_LAUNCH_FAILED;
+  {
+    const uint64_t R = p->rows, S = p->cols;
+    const uint64_t dims[4] = {S, R, uint64_t(kC), uint64_t(p->batch)};
+    const uint64_t strides[3] = {S * 2, R * S * 2, uint64_t(kC) * R * S * 2};
+    const uint32_t box[4] = {64, 1, kC, 1};
+    if (!make_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, x_cm, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  const PackedLayout L = PackedLayout::make(kC, kC);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  {
+    const uint64_t dims[2] = {kC, 2 * kC}, strides[1] = {kC * 2};
+    const uint32_t box[2] = {64, 256};
+    if (!make_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pk + L.w_out, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  const int grid = tl.tiles < sm_count(dev) ? tl.tiles : sm_count(dev);
+  cudaError_t e = launch_output_stage(
+      zmap, xmap, wmap, mask, reinterpret_cast<const float*>(pk + L.u_g),
+      reinterpret_cast<const float*>(pk + L.v_g), reinterpret_cast<const float*>(pk + L.u_o),
+      reinterpret_cast<const float*>(pk + L.v_o), out, p->out_dtype, tl, p->residual ? 1 : 0,
+      p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, p->eps_out, err, grid, stream);
+  return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
+}
+
+struct WsLayout {
+  size_t a, b, x, err, total;
+};
+
+WsLayout ws_layout(const ftm_problem* p) {
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t plane = size_t(p->batch) * kC * p->rows * p->cols * 2;
+  WsLayout w{};
+  w.a = 0;
+  w.b = up(plane);
+  w.x = w.b + up(plane);
+  w.err = w.x + up(plane);
+  w.total = w.err + 256;
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ftm_packed_params_bytes(int32_t c_z, int32_t c_h) {
+  return PackedLayout::make(c_z, c_h).total;
+}
+
+int ftm_pack_params(const void* const params[16], int32_t param_dtype, int32_t c_z, int32_t c_h,
+                    void* packed, ftm_stream_t stream) {
+  g_last_launches = 0;
+  if (!params || !packed) return FTM_BAD_ARGUMENT;
+  for (int i = 0; i < 16; ++i)
+    if (!params[i]) return FTM_BAD_ARGUMENT;
+  if (param_dtype != FTM_F16 && param_dtype != FTM_F32) return FTM_BAD_DTYPE;
+  if (c_z < 1 || c_h < 1 || c_z > 4096 || c_h > 4096) return FTM_BAD_SHAPE;
+  if (!aligned16(packed)) return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  cudaError_t e = launch_pack_params(params, param_dtype == FTM_F16 ? 1 : 0, c_z, c_h, packed,
+                                     reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return FTM_LAUNCH_FAILED;
+  g_last_launches = 1;
+  return FTM_OK;
+}
+
+size_t ftm_workspace_bytes(const ftm_problem* p) {
+  if (check_problem(p) != FTM_OK) return 0;
+  return ws_layout(p).total;
+}
+
+int* ftm_workspace_error_word(const ftm_problem* p, void* workspace) {
+  if (!workspace || check_problem(p) != FTM_OK) return nullptr;
+  return reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + ws_layout(p).err);
+}
+
+int ftm_trimul_fwd(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+                   void* out, void* workspace, size_t workspace_bytes, ftm_stream_t stream) {
+  g_last_launches = 0;
+  int st = check_problem(p);
+  if (st != FTM_OK) return st;
+  if (p->rows != p->cols) return FTM_BAD_SHAPE;  // row shards go through the stage calls
+  if (!z || !packed || !out) return FTM_BAD_ARGUMENT;
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(out) || (mask && !aligned16(mask)))
+    return FTM_BAD_ALIGN;
+  const WsLayout w = ws_layout(p);
+  if (!workspace || workspace_bytes < w.total) return FTM_BAD_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* err = reinterpret_cast<int*>(ws + w.err);
+  if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return FTM_LAUNCH_FAILED;
+  const int N = p->cols, L = p->batch * kC;
+  if ((st = stage_in(p, z, mask, packed, ws + w.a, ws + w.b, err, s, dev)) != FTM_OK) return st;
+  if ((st = stage_contract(ws + w.a, ws + w.b, ws + w.x, L, N, N, N, 1, err, s, dev)) != FTM_OK)
+    return st;
+  if ((st = stage_out(p, z, mask, ws + w.x, packed, out, err, s, dev)) != FTM_OK) return st;
+  g_last_launches = 3;
+  return FTM_OK;
+}
+
+int ftm_input_stage(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+                    void* a_cm, void* b_cm, int* err_word, ftm_stream_t stream) {
+  g_last_launches = 0;
+  int st = check_problem(p);
+  if (st != FTM_OK) return st;
+  if (!z || !packed || !a_cm || !b_cm || !err_word) return FTM_BAD_ARGUMENT;
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(a_cm) || !aligned16(b_cm) ||
+      (mask && !aligned16(mask)))
+    return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  st = stage_in(p, z, mask, packed, a_cm, b_cm, err_word, reinterpret_cast<cudaStream_t>(stream),
+                dev);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+int ftm_contraction(const void* A, const void* B, void* X, int32_t L, int32_t m, int32_t k,
+                    int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
+                    ftm_stream_t stream) {
+  g_last_launches = 0;
+  if (!A || !B || !X || !err_word) return FTM_BAD_ARGUMENT;
+  if (L < 1 || m < 1 || k < 1 || b_rows_per_block < 1 || b_blocks < 1) return FTM_BAD_SHAPE;
+  if (k % 8 != 0 || (b_rows_per_block * b_blocks) % 8 != 0) return FTM_BAD_SHAPE;
+  if (b_blocks > 1 && b_rows_per_block % kCtBN != 0) return FTM_BAD_SHAPE;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(X)) return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  const int st = stage_contract(A, B, X, L, m, k, b_rows_per_block, b_blocks, err_word,
+                                reinterpret_cast<cudaStream_t>(stream), dev);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+int ftm_output_stage(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
+                     const void* packed, void* out, int* err_word, ftm_stream_t stream) {
+  g_last_launches = 0;
+  int st = check_problem(p);
+  if (st != FTM_OK) return st;
+  if (!z || !x_cm || !packed || !out || !err_word) return FTM_BAD_ARGUMENT;
+  if (!aligned16(z) || !aligned16(x_cm) || !aligned16(packed) || !aligned16(out) ||
+      (mask && !aligned16(mask)))
+    return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  st = stage_out(p, z, mask, x_cm, packed, out, err_word, reinterpret_cast<cudaStream_t>(stream),
+                 dev);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+int ftm_check_error(const int* err_word, int* detail, ftm_stream_t stream) {
+  if (!err_word) return FTM_BAD_ARGUMENT;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return FTM_LAUNCH_FAILED;
+  int v = 0;
+  if (cudaMemcpy(&v, err_word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return FTM_LAUNCH_FAILED;
+  if (detail) *detail = v;
+  if (v != 0) {
+    cudaMemset(const_cast<int*>(err_word), 0, sizeof(int));
+    return FTM_TIMEOUT;
+  }
+  return FTM_OK;
+}
+
+const char* ftm_status_string(int status) {
+  switch (status) {
+    case FTM_OK: return "ok";
+    case FTM_BAD_SHAPE: return "unsupported shape (needs c_z == c_h == 128, N % 8 == 0)";
+    case FTM_BAD_DTYPE: return "unsupported dtype";
+    case FTM_BAD_ALIGN: return "pointer not 16-byte aligned (workspace: 256-byte)";
+    case FTM_UNSUPPORTED_ARCH: return "device is not an sm_100 (B200-class) GPU";
+    case FTM_LAUNCH_FAILED: return "kernel launch or tensor-map encoding failed";
+    case FTM_TIMEOUT: return "a bounded device-side wait expired";
+    case FTM_BAD_WORKSPACE: return "workspace missing or too small";
+    case FTM_BAD_ARGUMENT: return "invalid argument";
+    default: return "unknown status";
+  }
+}
+
+int ftm_device_supported(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess)
+    return 0;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess)
+    return 0;
+  return (major == 10 && minor == 0) ? 1 : 0;
+}
+
+int ftm_last_launch_count(void) { return g_last_launches; }
+
+}  // extern "C"

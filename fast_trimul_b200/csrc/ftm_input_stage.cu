@@ -1,0 +1,300 @@
+// Input stage of the triangle multiplicative update (sm_100a).
+//
+// Reference work replaced (fast_trimul/_kernels.py:520-524 plus the permute copies
+// of :138-139 / :155-156):   z_n = LayerNorm(z*mask);  a = (z_n W_ap + b_ap) *
+// sigmoid(z_n W_ag + b_ag);  b likewise;  a, b written channel-major.
+//
+// One persistent CTA per SM. Per tile of 128 positions:
+//   warp 0      TMA: z tile (2 x 16 KB, 128B-swizzled, K-major) into a ring slot;
+//               the folded weight W' = [W_ap;W_ag;W_bp;W_bg]*diag(gamma_in) (512 x 128
+//               fp16, 128 KB) is loaded once and stays resident.
+//   warps 2-5   per row: fp32 mean/variance of z*mask (the LayerNorm statistics),
+//               bf16 -> fp16 in place when z is bf16, then mark the slot ready.
+//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) x 8 per half into
+//               TMEM: half 0 = [a_p | a_g] (256 columns), half 1 = [b_p | b_g].
+//   warps 6-9   TMEM -> registers; proj = m*rstd*(acc - mean*rowsum(W')) + (W beta + b);
+//               a = proj_p * sigmoid(proj_g); fp16 stores to a_cm[b][c][u][v].
+// The two TMEM halves are separate 256-column slots, so the MMA of tile t+1's a-half
+// overlaps the epilogue of tile t's b-half.
+#include "ftm_kernels.h"
+
+namespace ftm {
+
+namespace {
+
+constexpr int kZTile = 128 * kC * 2;          // 32 KB fp16 z tile
+constexpr int kWBytes = 4 * kC * kC * 2;      // 128 KB
+constexpr int kOffW = 0;
+constexpr int kOffZ = kOffW + kWBytes;
+constexpr int kOffStats = kOffZ + kInBufs * kZTile;
+constexpr int kOffUV = kOffStats + kInBufs * 128 * 8;
+constexpr int kOffBar = kOffUV + 2 * 4 * kC * 4;
+constexpr int kNumBars = 1 + 3 * kInBufs + 4 + 1;
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffTmem + 16 + 1024;  // + alignment slack
+
+__global__ void __launch_bounds__(kInThreads, 1)
+input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
+                   const __grid_constant__ CUtensorMap wmap, const float* __restrict__ mask,
+                   const float* __restrict__ u_in, const float* __restrict__ v_in,
+                   __half* __restrict__ a_cm, __half* __restrict__ b_cm, PosTiling tl,
+                   int incoming, int z_bf16, float eps, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sW = smem + kOffW;
+  uint8_t* sZ = smem + kOffZ;
+  float2* sStats = reinterpret_cast<float2*>(smem + kOffStats);
+  float* sU = reinterpret_cast<float*>(smem + kOffUV);
+  float* sV = sU + 4 * kC;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* w_full = bars;
+  uint64_t* z_full = bars + 1;
+  uint64_t* a_ready = z_full + kInBufs;
+  uint64_t* buf_empty = a_ready + kInBufs;
+  uint64_t* tmem_full = buf_empty + kInBufs;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* mma_drain = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(w_full, 1);
+    for (int s = 0; s < kInBufs; ++s) {
+      mbar_init(&z_full[s], 1);
+      mbar_init(&a_ready[s], 128);
+      mbar_init(&buf_empty[s], 1 + 4);  // MMA commit + 4 epilogue warps (stats read)
+    }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&tmem_full[h], 1);
+      mbar_init(&tmem_empty[h], 4);
+    }
+    mbar_init(mma_drain, 1);
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 4 * kC; i += blockDim.x) {
+    sU[i] = u_in[i];
+    sV[i] = v_in[i];
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int ntiles = tl.tiles;
+  const size_t plane = static_cast<size_t>(tl.R) * tl.S;  // positions per (batch, channel)
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&zmap);
+      tma_prefetch_desc(&wmap);
+      mbar_arrive_expect_tx(w_full, kWBytes);
+      for (int kc = 0; kc < 2; ++kc)
+        for (int h = 0; h < 2; ++h)
+          tma_load_2d(&wmap, w_full, sW + kc * 65536 + h * 32768, kc * 64, h * 256);
+      int it = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int s = it % kInBufs;
+        const uint32_t ph = (it / kInBufs) & 1;
+        if (!mbar_wait(&buf_empty[s], ph ^ 1, err, err_code(KERNEL_INPUT, ROLE_PRODUCER, 1))) break;
+        int b, u0, v0;
+        tl.tile(t, b, u0, v0);
+        uint8_t* dst = sZ + s * kZTile;
+        mbar_arrive_expect_tx(&z_full[s], kZTile);
+        tma_load_4d(&zmap, &z_full[s], dst, 0, v0, u0, b);
+        tma_load_4d(&zmap, &z_full[s], dst + kZTile / 2, 64, v0, u0, b);
+      }
+      // copies still in flight must land before the CTA exits
+      for (int i = (it > kInBufs ? it - kInBufs : 0); i < it; ++i)
+        mbar_wait_drain(&z_full[i % kInBufs], (i / kInBufs) & 1);
+      mbar_wait_drain(w_full, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(0, 128, 256, 0, 0);
+      const uint32_t wbase = smem_u32(sW);
+      const uint32_t zbase = smem_u32(sZ);
+      bool ok = mbar_wait(w_full, 0, err, err_code(KERNEL_INPUT, ROLE_MMA, 1));
+      tc_fence_after();
+      int it = 0;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
+        const int s = it % kInBufs;
+        if (!mbar_wait(&a_ready[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_MMA, 2))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t abase = zbase + s * kZTile;
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&tmem_empty[h], (it & 1) ^ 1, err, err_code(KERNEL_INPUT, ROLE_MMA, 3))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + h * 256;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = kmajor_desc(abase + (kk >> 2) * (kZTile / 2) + (kk & 3) * 32);
+            const uint64_t bd = kmajor_desc(wbase + (kk >> 2) * 65536 + h * 32768 + (kk & 3) * 32);
+            umma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&tmem_full[h]);
+        }
+        if (!ok) break;
+        umma_commit(&buf_empty[s]);
+      }
+      // make sure every MMA this thread issued has finished before TMEM is freed
+      umma_commit(mma_drain);
+      mbar_wait_drain(mma_drain, 0);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------- LayerNorm statistics
+    const int row = threadIdx.x - 64;  // 0..127
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int s = it % kInBufs;
+      if (!mbar_wait(&z_full[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_TRANSFORM, 1)))
+        break;
+      int b, u0, v0;
+      tl.tile(t, b, u0, v0);
+      const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
+      const bool valid = (u < tl.R) && (v < tl.S);
+      uint8_t* zt = sZ + s * kZTile;
+      uint4 raw[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        raw[q] = *reinterpret_cast<const uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7));
+      // single-pass statistics shifted by the row's first value (numerically stable)
+      float shift, sum = 0.f, sq = 0.f;
+      if (z_bf16) {
+        shift = __bfloat162float(reinterpret_cast<const __nv_bfloat162*>(&raw[0])->x);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&raw[q]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(p[e]);
+            const float d0 = f.x - shift, d1 = f.y - shift;
+            sum += d0 + d1;
+            sq += d0 * d0 + d1 * d1;
+            w[e] = pack_half2(f.x, f.y);  // exact for bf16 values inside fp16 range
+          }
+        }
+      } else {
+        shift = __half2float(reinterpret_cast<const __half2*>(&raw[0])->x);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const __half2* p = reinterpret_cast<const __half2*>(&raw[q]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(p[e]);
+            const float d0 = f.x - shift, d1 = f.y - shift;
+            sum += d0 + d1;
+            sq += d0 * d0 + d1 * d1;
+          }
+        }
+      }
+      const float inv_c = 1.0f / kC;
+      const float dm = sum * inv_c;
+      const float mean = shift + dm;
+      const float var = fmaxf(sq * inv_c - dm * dm, 0.f);
+      float m = 0.f;
+      if (valid) {
+        if (mask) {
+          const size_t zi = incoming ? (static_cast<size_t>(b) * tl.R + v) * tl.S + u
+                                     : (static_cast<size_t>(b) * tl.R + u) * tl.S + v;
+          m = __ldg(mask + zi);
+        } else {
+          m = 1.f;
+        }
+      }
+      // LayerNorm(m*z) = m*rstd*(z - mean), rstd = 1/sqrt(m^2 var + eps)
+      const float rstd = rsqrtf(m * m * var + eps);
+      const float sa = m * rstd;
+      sStats[s * 128 + row] = make_float2(sa, -sa * mean);
+      if (z_bf16) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          *reinterpret_cast<uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7)) = raw[q];
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&a_ready[s]);
+    }
+  } else {
+    // ----------------------------------------------------------------- epilogue
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(sub * 32) << 16);
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
+      const int s = it % kInBufs;
+      int b, u0, v0;
+      tl.tile(t, b, u0, v0);
+      const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
+      const bool valid = (u < tl.R) && (v < tl.S);
+      const size_t pos = static_cast<size_t>(u) * tl.S + v;
+      if (!mbar_wait_warp(&a_ready[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_EPILOGUE, 1))) break;
+      const float2 st = sStats[s * 128 + row];
+      for (int h = 0; h < 2; ++h) {
+        if (!mbar_wait_warp(&tmem_full[h], it & 1, err, err_code(KERNEL_INPUT, ROLE_EPILOGUE, 2))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        __half* dst = (h == 0 ? a_cm : b_cm) + static_cast<size_t>(b) * kC * plane + pos;
+        const float* up = sU + h * 256;
+        const float* vp = sV + h * 256;
+#pragma unroll 1
+        for (int cb = 0; cb < 4; ++cb) {
+          float p[32], g[32];
+          tmem_ld32(lane_base + h * 256 + cb * 32, p);
+          tmem_ld32(lane_base + h * 256 + 128 + cb * 32, g);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = cb * 32 + i;
+            const float pv = fmaf(st.x, p[i], fmaf(st.y, up[c], vp[c]));
+            const float gv = fmaf(st.x, g[i], fmaf(st.y, up[128 + c], vp[128 + c]));
+            if (valid) dst[static_cast<size_t>(c) * plane] = __float2half_rn(pv * sigmoidf_fast(gv));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[h]);
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&buf_empty[s]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace
+
+size_t input_stage_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap, const float* mask,
+                               const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
+                               const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
+                               int grid, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, mask, u_in, v_in, a_cm,
+                                                               b_cm, tl, incoming, z_bf16, eps, err);
+  return cudaGetLastError();
+}
+
+}  // namespace ftm

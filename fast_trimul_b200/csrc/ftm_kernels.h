@@ -1,0 +1,64 @@
+// Internal launch interface between the C ABI (ftm_api.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ftm_common.cuh"
+
+namespace ftm {
+
+// Packed parameter buffer (built by ftm_pack_params), byte offsets for C = c_z = c_h.
+struct PackedLayout {
+  size_t w_in, w_out, u_in, v_in, u_g, v_g, u_o, v_o, total;
+  static PackedLayout make(int c_z, int c_h) {
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    PackedLayout L{};
+    size_t off = 0;
+    L.w_in = off;  off = up(off + size_t(4) * c_h * c_z * 2);            // [a_p;a_g;b_p;b_g] x c_z, fp16
+    L.w_out = off; off = up(off + size_t(c_z) * c_z * 2 + size_t(c_z) * c_h * 2);  // [W_g'; W_o'] fp16
+    L.u_in = off;  off = up(off + size_t(4) * c_h * 4);
+    L.v_in = off;  off = up(off + size_t(4) * c_h * 4);
+    L.u_g = off;   off = up(off + size_t(c_z) * 4);
+    L.v_g = off;   off = up(off + size_t(c_z) * 4);
+    L.u_o = off;   off = up(off + size_t(c_z) * 4);
+    L.v_o = off;   off = up(off + size_t(c_z) * 4);
+    L.total = off;
+    return L;
+  }
+};
+
+constexpr int kC = 128;            // c_z == c_h supported by the tensor-core kernels
+constexpr int kInThreads = 320;    // producer, MMA, 4 transform, 4 epilogue warps
+constexpr int kInBufs = 2;
+constexpr int kOutThreads = 320;
+constexpr int kOutBufs = 2;
+constexpr int kCtThreads = 192;    // producer, MMA, 4 epilogue warps
+constexpr int kCtStages = 4;
+constexpr int kCtBM = 128, kCtBN = 256, kCtBK = 64;
+
+size_t input_stage_smem_bytes();
+size_t output_stage_smem_bytes();
+size_t contraction_smem_bytes();
+
+cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap, const float* mask,
+                               const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
+                               const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
+                               int grid, cudaStream_t stream);
+
+cudaError_t launch_contraction(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X, int L,
+                               int M, int N, int K, int rows_per_block, int* err, int grid,
+                               cudaStream_t stream);
+
+cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
+                                const CUtensorMap& wmap, const float* mask, const float* u_g,
+                                const float* v_g, const float* u_o, const float* v_o, void* out,
+                                int out_dtype, const PosTiling& tl, int residual, int z_bf16,
+                                float eps_in, float eps_out, int* err, int grid,
+                                cudaStream_t stream);
+
+cudaError_t launch_pack_params(const void* const params[16], int param_is_f16, int c_z, int c_h,
+                               void* packed, cudaStream_t stream);
+
+}  // namespace ftm

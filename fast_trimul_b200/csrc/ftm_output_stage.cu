@@ -1,0 +1,367 @@
+// Output stage of the triangle multiplicative update (sm_100a).
+//
+// Reference work replaced (fast_trimul/_kernels.py:526-530 and the mask / cast glue
+// of functional.py:24-26):
+//   x_n = LayerNorm_ch(x);  g = sigmoid(LN_cz(z*mask) W_g + b_g);
+//   delta = g * (x_n W_o + b_o);  out = ((residual ? z*mask : 0) + delta) * mask.
+//
+// One persistent CTA per SM, 128 positions per tile, two ring slots:
+//   warp 0     TMA: z tile (K-major, 128B swizzle) and the x tile straight from the
+//              channel-major x (MN-major operand: 64-position atoms x 128 channels),
+//              plus the resident folded weights [W_g diag(gamma_in); W_o diag(gamma_out)].
+//   warps 2-5  per row: LayerNorm statistics of z*mask and of x (fp32), bf16 -> fp16
+//              of z in place when needed.
+//   warp 1     tcgen05.mma: TMEM[0:128) = z W_g'^T (K-major A), TMEM[128:256) =
+//              x W_o'^T (MN-major A); two 256-column accumulators alternate tiles.
+//   warps 6-9  epilogue: fold the statistics back in, gate, residual, mask, store.
+#include "ftm_kernels.h"
+
+namespace ftm {
+
+namespace {
+
+constexpr int kHalfTile = 128 * 64 * 2;   // 16 KB
+constexpr int kZTile = 2 * kHalfTile;     // 32 KB
+constexpr int kXTile = 2 * kHalfTile;     // 32 KB
+constexpr int kSlot = kZTile + kXTile;
+constexpr int kWBytes = 2 * kC * kC * 2;  // 64 KB
+constexpr int kOffW = 0;
+constexpr int kOffSlots = kOffW + kWBytes;
+constexpr int kOffStats = kOffSlots + kOutBufs * kSlot;
+constexpr int kOffMask = kOffStats + kOutBufs * 128 * 16;
+constexpr int kOffUV = kOffMask + kOutBufs * 128 * 4;
+constexpr int kOffBar = kOffUV + 4 * kC * 4;
+constexpr int kNumBars = 1 + 3 * kOutBufs + 4 + 1;
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffTmem + 16 + 1024;
+
+template <int OUT_DT>
+__device__ __forceinline__ void store_out32(void* out, size_t elem, const float (&r)[32]) {
+  if (OUT_DT == 0) {  // fp32
+    float4* p = reinterpret_cast<float4*>(static_cast<float*>(out) + elem);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) p[q] = make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+  } else {
+    uint4* p = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + elem);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 o;
+      if (OUT_DT == 1) {
+        o.x = pack_half2(r[8 * q + 0], r[8 * q + 1]);
+        o.y = pack_half2(r[8 * q + 2], r[8 * q + 3]);
+        o.z = pack_half2(r[8 * q + 4], r[8 * q + 5]);
+        o.w = pack_half2(r[8 * q + 6], r[8 * q + 7]);
+      } else {
+        o.x = pack_bf162(r[8 * q + 0], r[8 * q + 1]);
+        o.y = pack_bf162(r[8 * q + 2], r[8 * q + 3]);
+        o.z = pack_bf162(r[8 * q + 4], r[8 * q + 5]);
+        o.w = pack_bf162(r[8 * q + 6], r[8 * q + 7]);
+      }
+      p[q] = o;
+    }
+  }
+}
+
+template <int OUT_DT>
+__global__ void __launch_bounds__(kOutThreads, 1)
+output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
+                    const __grid_constant__ CUtensorMap xmap,
+                    const __grid_constant__ CUtensorMap wmap, const float* __restrict__ mask,
+                    const float* __restrict__ u_g, const float* __restrict__ v_g,
+                    const float* __restrict__ u_o, const float* __restrict__ v_o,
+                    void* __restrict__ out, PosTiling tl, int residual, int z_bf16,
+                    float eps_in, float eps_out, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sW = smem + kOffW;
+  uint8_t* sSlots = smem + kOffSlots;
+  float4* sStats = reinterpret_cast<float4*>(smem + kOffStats);
+  float* sMask = reinterpret_cast<float*>(smem + kOffMask);
+  float* sUg = reinterpret_cast<float*>(smem + kOffUV);
+  float* sVg = sUg + kC;
+  float* sUo = sVg + kC;
+  float* sVo = sUo + kC;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* w_full = bars;
+  uint64_t* full = bars + 1;
+  uint64_t* a_ready = full + kOutBufs;
+  uint64_t* buf_empty = a_ready + kOutBufs;
+  uint64_t* tmem_full = buf_empty + kOutBufs;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* mma_drain = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(w_full, 1);
+    for (int s = 0; s < kOutBufs; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&a_ready[s], 128);
+      mbar_init(&buf_empty[s], 4);  // epilogue warps (they finish after the MMA read)
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4);
+    }
+    mbar_init(mma_drain, 1);
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < kC; i += blockDim.x) {
+    sUg[i] = u_g[i];
+    sVg[i] = v_g[i];
+    sUo[i] = u_o[i];
+    sVo[i] = v_o[i];
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int ntiles = tl.tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&zmap);
+      tma_prefetch_desc(&xmap);
+      tma_prefetch_desc(&wmap);
+      mbar_arrive_expect_tx(w_full, kWBytes);
+      for (int kc = 0; kc < 2; ++kc) tma_load_2d(&wmap, w_full, sW + kc * 32768, kc * 64, 0);
+      int it = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int s = it % kOutBufs;
+        if (!mbar_wait(&buf_empty[s], ((it / kOutBufs) & 1) ^ 1, err,
+                       err_code(KERNEL_OUTPUT, ROLE_PRODUCER, 1)))
+          break;
+        int b, u0, v0;
+        tl.tile(t, b, u0, v0);
+        uint8_t* zs = sSlots + s * kSlot;
+        uint8_t* xs = zs + kZTile;
+        mbar_arrive_expect_tx(&full[s], kSlot);
+        tma_load_4d(&zmap, &full[s], zs, 0, v0, u0, b);
+        tma_load_4d(&zmap, &full[s], zs + kHalfTile, 64, v0, u0, b);
+        for (int h = 0; h < 2; ++h) {
+          const int jj = tl.vt == 128 ? v0 + 64 * h : v0;
+          const int ii = tl.vt == 128 ? u0 : u0 + h;
+          tma_load_4d(&xmap, &full[s], xs + h * kHalfTile, jj, ii, 0, b);
+        }
+      }
+      for (int i = (it > kOutBufs ? it - kOutBufs : 0); i < it; ++i)
+        mbar_wait_drain(&full[i % kOutBufs], (i / kOutBufs) & 1);
+      mbar_wait_drain(w_full, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_z = idesc_f16(0, 128, 128, 0, 0);
+      constexpr uint32_t idesc_x = idesc_f16(0, 128, 128, 1, 0);  // A (x) is MN-major
+      const uint32_t wbase = smem_u32(sW);
+      bool ok = mbar_wait(w_full, 0, err, err_code(KERNEL_OUTPUT, ROLE_MMA, 1));
+      tc_fence_after();
+      int it = 0;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
+        const int s = it % kOutBufs;
+        const uint32_t ph = (it / kOutBufs) & 1;
+        if (!mbar_wait(&a_ready[s], ph, err, err_code(KERNEL_OUTPUT, ROLE_MMA, 2)) ||
+            !mbar_wait(&tmem_empty[s], ph ^ 1, err, err_code(KERNEL_OUTPUT, ROLE_MMA, 3))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t zs = smem_u32(sSlots + s * kSlot);
+        const uint32_t xs = zs + kZTile;
+        const uint32_t d = tmem_base + s * 256;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // gate projection: z (K-major) x W_g'
+          const uint64_t ad = kmajor_desc(zs + (kk >> 2) * kHalfTile + (kk & 3) * 32);
+          const uint64_t bd = kmajor_desc(wbase + (kk >> 2) * 32768 + (kk & 3) * 32);
+          umma_f16(d, ad, bd, idesc_z, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // output projection: x (MN-major) x W_o'
+          const uint64_t ad = sw128_desc(xs + kk * 2048, kHalfTile, 1024);
+          const uint64_t bd = kmajor_desc(wbase + (kk >> 2) * 32768 + 16384 + (kk & 3) * 32);
+          umma_f16(d + 128, ad, bd, idesc_x, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&tmem_full[s]);
+      }
+      umma_commit(mma_drain);
+      mbar_wait_drain(mma_drain, 0);
+    }
+  } else if (warp < 6) {
+    const int row = threadIdx.x - 64;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int s = it % kOutBufs;
+      if (!mbar_wait(&full[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
+        break;
+      int b, u0, v0;
+      tl.tile(t, b, u0, v0);
+      const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
+      const bool valid = (u < tl.R) && (v < tl.S);
+      uint8_t* zs = sSlots + s * kSlot;
+      const uint8_t* xs = zs + kZTile;
+      // z row statistics (+ bf16 -> fp16 in place)
+      uint4 raw[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        raw[q] = *reinterpret_cast<const uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7));
+      float shift, sum = 0.f, sq = 0.f;
+      if (z_bf16) {
+        shift = __bfloat162float(reinterpret_cast<const __nv_bfloat162*>(&raw[0])->x);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&raw[q]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(p[e]);
+            const float d0 = f.x - shift, d1 = f.y - shift;
+            sum += d0 + d1;
+            sq += d0 * d0 + d1 * d1;
+            w[e] = pack_half2(f.x, f.y);
+          }
+        }
+      } else {
+        shift = __half2float(reinterpret_cast<const __half2*>(&raw[0])->x);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const __half2* p = reinterpret_cast<const __half2*>(&raw[q]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(p[e]);
+            const float d0 = f.x - shift, d1 = f.y - shift;
+            sum += d0 + d1;
+            sq += d0 * d0 + d1 * d1;
+          }
+        }
+      }
+      const float inv_c = 1.0f / kC;
+      float dm = sum * inv_c;
+      const float mean_z = shift + dm;
+      const float var_z = fmaxf(sq * inv_c - dm * dm, 0.f);
+      // x column statistics: element (c, row) of the MN-major x tile
+      const int h = row >> 6, e = row & 63;
+      const uint8_t* xcol = xs + h * kHalfTile + (e & 7) * 2;
+      const float xshift = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(0, e >> 3)));
+      float xs1 = 0.f, xs2 = 0.f;
+#pragma unroll 8
+      for (int c = 0; c < kC; ++c) {
+        const float xv = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c, e >> 3)));
+        const float d0 = xv - xshift;
+        xs1 += d0;
+        xs2 += d0 * d0;
+      }
+      dm = xs1 * inv_c;
+      const float mean_x = xshift + dm;
+      const float var_x = fmaxf(xs2 * inv_c - dm * dm, 0.f);
+      float m = 0.f;
+      if (valid) m = mask ? __ldg(mask + (static_cast<size_t>(b) * tl.R + u) * tl.S + v) : 1.f;
+      const float rz = rsqrtf(m * m * var_z + eps_in);
+      const float sa = m * rz;
+      const float rx = rsqrtf(var_x + eps_out);
+      sStats[s * 128 + row] = make_float4(sa, -sa * mean_z, rx, -rx * mean_x);
+      sMask[s * 128 + row] = m;
+      if (z_bf16) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          *reinterpret_cast<uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7)) = raw[q];
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&a_ready[s]);
+    }
+  } else {
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(sub * 32) << 16);
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int s = it % kOutBufs;
+      const uint32_t ph = (it / kOutBufs) & 1;
+      if (!mbar_wait_warp(&a_ready[s], ph, err, err_code(KERNEL_OUTPUT, ROLE_EPILOGUE, 1)) ||
+          !mbar_wait_warp(&tmem_full[s], ph, err, err_code(KERNEL_OUTPUT, ROLE_EPILOGUE, 2)))
+        break;
+      tc_fence_after();
+      int b, u0, v0;
+      tl.tile(t, b, u0, v0);
+      const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
+      const bool valid = (u < tl.R) && (v < tl.S);
+      const size_t elem0 = ((static_cast<size_t>(b) * tl.R + u) * tl.S + v) * kC;
+      const float4 st = sStats[s * 128 + row];
+      const float m = sMask[s * 128 + row];
+      const uint8_t* zs = sSlots + s * kSlot;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float ga[32], oa[32];
+        tmem_ld32(lane_base + s * 256 + cb * 32, ga);
+        tmem_ld32(lane_base + s * 256 + 128 + cb * 32, oa);
+        float zv[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = cb * 4 + q;  // 16-byte chunk of the 256-byte z row
+          const uint4 zz = *reinterpret_cast<const uint4*>(zs + (chunk >> 3) * kHalfTile +
+                                                           sw128_off(row, chunk & 7));
+          const __half2* hp = reinterpret_cast<const __half2*>(&zz);
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const float2 f = __half22float2(hp[e2]);
+            zv[q * 8 + 2 * e2] = f.x;
+            zv[q * 8 + 2 * e2 + 1] = f.y;
+          }
+        }
+        float r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int n = cb * 32 + i;
+          const float g = sigmoidf_fast(fmaf(st.x, ga[i], fmaf(st.y, sUg[n], sVg[n])));
+          const float o = fmaf(st.z, oa[i], fmaf(st.w, sUo[n], sVo[n]));
+          const float dlt = g * o;
+          r[i] = (residual ? fmaf(m, zv[i], dlt) : dlt) * m;
+        }
+        if (valid) store_out32<OUT_DT>(out, elem0 + cb * 32, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&tmem_empty[s]);
+        mbar_arrive(&buf_empty[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace
+
+size_t output_stage_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
+                                const CUtensorMap& wmap, const float* mask, const float* u_g,
+                                const float* v_g, const float* u_o, const float* v_o, void* out,
+                                int out_dtype, const PosTiling& tl, int residual, int z_bf16,
+                                float eps_in, float eps_out, int* err, int grid,
+                                cudaStream_t stream) {
+  auto go = [&](auto kern) -> cudaError_t {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kOutThreads, kSmemBytes, stream>>>(zmap, xmap, wmap, mask, u_g, v_g, u_o, v_o, out,
+                                                    tl, residual, z_bf16, eps_in, eps_out, err);
+    return cudaGetLastError();
+  };
+  switch (out_dtype) {
+    case 0: return go(output_stage_kernel<0>);
+    case 1: return go(output_stage_kernel<1>);
+    case 2: return go(output_stage_kernel<2>);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace ftm

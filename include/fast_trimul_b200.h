@@ -1,0 +1,130 @@
+/*
+ * fast_trimul_b200 -- C ABI of the B200 (sm_100a) triangle multiplicative update.
+ *
+ * The drop-in boundary for the reference's operator path. The reference
+ * (fast_trimul, pure Python) reaches its GPU code through
+ *   functional.triangle_multiplication(z, params, mask)        functional.py:7-26
+ *   -> TriangleMultiplicativeUpdateKernelFused._forward_kernels _kernels.py:519-530
+ * and the backend plug-in `execute(inp, params)`               backends/cuda_cute.py:38-39
+ * Each entry point below names the reference code it replaces. Plain pointers and
+ * sizes only; no framework types. All calls are asynchronous on `stream`, allocate
+ * no memory and do not synchronise; the caller owns every buffer.
+ *
+ * Semantics follow the reference exactly: z is multiplied by the pair mask BEFORE the
+ * input LayerNorm (functional.py:21-22), the output is multiplied by the mask again
+ * (:25-26), residual=1 returns z*mask + delta (_kernels.py:547). Internal arithmetic is
+ * fp16 storage with fp32 accumulation and fp32 LayerNorm statistics, as in the
+ * reference's fp16 kernels (ops/triangle.py:39).
+ */
+#ifndef FAST_TRIMUL_B200_H
+#define FAST_TRIMUL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ftm_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  FTM_OK = 0,
+  FTM_BAD_SHAPE = 1,        /* unsupported B/N/c_z/c_h (reference guard: context.py:41-55) */
+  FTM_BAD_DTYPE = 2,
+  FTM_BAD_ALIGN = 3,        /* a pointer is not 16-byte aligned */
+  FTM_UNSUPPORTED_ARCH = 4, /* device is not sm_100 */
+  FTM_LAUNCH_FAILED = 5,
+  FTM_TIMEOUT = 6,          /* a bounded device-side wait expired (see ftm_check_error) */
+  FTM_BAD_WORKSPACE = 7,    /* workspace missing or smaller than ftm_workspace_bytes() */
+  FTM_BAD_ARGUMENT = 8
+} ftm_status;
+
+typedef enum { FTM_F32 = 0, FTM_F16 = 1, FTM_BF16 = 2 } ftm_dtype;
+typedef enum { FTM_OUTGOING = 0, FTM_INCOMING = 1 } ftm_mode;
+
+/* One forward problem. z is (batch, rows, cols, c_z) row-major; a full problem has
+ * rows == cols == N. A row shard of an outgoing problem (multi-GPU) has rows = N/P. */
+typedef struct {
+  int32_t batch;     /* B */
+  int32_t rows;      /* R: rows of z in this call */
+  int32_t cols;      /* S: N */
+  int32_t c_z;       /* pair channels (128) */
+  int32_t c_h;       /* hidden channels (128) */
+  int32_t mode;      /* ftm_mode */
+  int32_t residual;  /* 1: z*mask + delta, 0: delta only */
+  int32_t z_dtype;   /* FTM_F16 or FTM_BF16 (fp32 callers convert to fp16 first, as
+                        functional.py:23 does) */
+  int32_t out_dtype; /* FTM_F16, FTM_BF16 or FTM_F32 */
+  float eps_in;      /* norm_in eps (nn.LayerNorm default 1e-5) */
+  float eps_out;     /* norm_out eps */
+} ftm_problem;
+
+/* ---- parameters --------------------------------------------------------------
+ * Replaces the per-call weight handling of _kernels.py:202-223 (`torch.cat` of the
+ * [proj; gate] weights on every call) and KernelLinear's prebinding (:165-199):
+ * parameters are packed once into a device buffer that all calls read.
+ *
+ * `params` holds 16 device pointers in the reference's _params() order
+ * (_kernels.py:512-517): norm_in.{weight,bias}, norm_out.{weight,bias},
+ * proj_a, gate_a, proj_b, gate_b, proj_g, proj_out as {weight (out x in), bias}.
+ * param_dtype is FTM_F16 (the reference module is .half(), ops/triangle.py:39) or
+ * FTM_F32. The LayerNorm affine is folded into the weights:
+ *   LN(x) W^T + b = rstd*(x (W diag(gamma))^T - mean*rowsum(W diag(gamma))) + W beta + b. */
+size_t ftm_packed_params_bytes(int32_t c_z, int32_t c_h);
+int ftm_pack_params(const void* const params[16], int32_t param_dtype, int32_t c_z, int32_t c_h,
+                    void* packed, ftm_stream_t stream);
+
+/* ---- whole forward ----------------------------------------------------------
+ * Replaces functional.triangle_multiplication -> _forward_kernels
+ * (functional.py:7-26, _kernels.py:519-530). mask is (batch, rows, cols) fp32 or
+ * NULL. out has z's shape in out_dtype. workspace: >= ftm_workspace_bytes(p),
+ * 256-byte aligned (holds a, b, x in fp16 channel-major and the error word). */
+size_t ftm_workspace_bytes(const ftm_problem* p);
+int ftm_trimul_fwd(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+                   void* out, void* workspace, size_t workspace_bytes, ftm_stream_t stream);
+
+/* ---- the three stages (for callers that interleave communication) -----------
+ * Input stage: LayerNorm(z*mask) -> [a_p|a_g|b_p|b_g] projection on the tensor cores
+ * -> sigmoid gating, written fp16 channel-major: a_cm[b][c][u][v] with (u,v) = (i,k)
+ * for outgoing and (k,i) transposed for incoming, so the contraction always reads
+ * K-major operands. Replaces layer_norm + _proj_gate + gate + permute copies
+ * (_kernels.py:520-524, :138-139, :155-156). */
+int ftm_input_stage(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+                    void* a_cm, void* b_cm, int* err_word, ftm_stream_t stream);
+
+/* Contraction: for l in [0, L): X[l][i][j] = sum_k A[l][i][k] * B[l][j][k]
+ * (fp16 in, fp32 accumulate, fp16 out). A is (L, m, k) row-major; B is stored as
+ * `b_blocks` blocks of (L, b_rows_per_block, k), block-major (what an all-gather of
+ * per-rank row shards produces), so B row j lives in block j / b_rows_per_block.
+ * X is (L, m, n) with n = b_blocks * b_rows_per_block. Replaces outgoing()/incoming()
+ * (_kernels.py:131-162). Requires k % 8 == 0 and, when b_blocks > 1,
+ * b_rows_per_block % 256 == 0. */
+int ftm_contraction(const void* A, const void* B, void* X, int32_t L, int32_t m, int32_t k,
+                    int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
+                    ftm_stream_t stream);
+
+/* Output stage: LayerNorm over c_h of x (channel-major fp16), the c_h -> c_z projection,
+ * sigmoid(z_n W_g + b_g) gate, residual and mask, stored in out_dtype. Replaces
+ * layer_norm + KernelLinear.raw x2 + gated_residual/gate + the mask/cast glue
+ * (_kernels.py:526-530, functional.py:24-26). */
+int ftm_output_stage(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
+                     const void* packed, void* out, int* err_word, ftm_stream_t stream);
+
+/* ---- status -------------------------------------------------------------- */
+/* Synchronise `stream`, read the device error word of a workspace (or any err_word
+ * passed to a stage) and clear it: FTM_OK, or FTM_TIMEOUT when a bounded device wait
+ * expired (the failing kernel/role/site is stored in *detail when non-NULL). */
+int ftm_check_error(const int* err_word, int* detail, ftm_stream_t stream);
+/* Address of the error word inside a workspace laid out for `p`. */
+int* ftm_workspace_error_word(const ftm_problem* p, void* workspace);
+const char* ftm_status_string(int status);
+/* 1 if `device` is an sm_100 GPU these kernels run on, else 0. */
+int ftm_device_supported(int device);
+/* Number of kernels the last successful ftm_trimul_fwd / stage call launched. */
+int ftm_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FAST_TRIMUL_B200_H */

@@ -1,0 +1,186 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the CPU oracle.
+
+Tolerance (stated by the north star): max-abs <= 2e-2 and mean-relative <= 1e-3
+against an fp32 reference of the same fp16 weights, measured on fp32 output (the
+kernels can write fp32 directly; bf16 output rounding alone is ~1.4e-3 mean-rel).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import MAX_ABS, MEAN_REL, compare, make_layer, make_mask, oracle_out
+
+pytestmark = pytest.mark.gpu
+
+needs_gpu = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
+
+
+def _native(m, z, mask, out_dtype=torch.float32):
+    from fast_trimul_b200 import _lib
+    n0 = _lib.stats["kernel_launches"]
+    with torch.no_grad():
+        out = m._impl._forward_native(z, mask, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert _lib.stats["kernel_launches"] - n0 == 3, "native path did not launch its kernels"
+    return out
+
+
+CASES = [
+    # (mode, B, N, residual, mask kind, z dtype)
+    ("outgoing", 1, 64, True, None, torch.float32),
+    ("incoming", 1, 64, True, None, torch.float32),
+    ("outgoing", 1, 8, True, "tail", torch.bfloat16),
+    ("incoming", 1, 16, False, None, torch.float16),
+    ("outgoing", 2, 24, False, "pad", torch.bfloat16),
+    ("incoming", 2, 40, True, "pad", torch.bfloat16),
+    ("outgoing", 1, 72, False, "tail", torch.float32),
+    ("incoming", 1, 136, True, "tail", torch.bfloat16),
+    ("outgoing", 1, 200, True, "frac", torch.float16),
+    ("incoming", 1, 256, True, "tail", torch.bfloat16),     # config C2
+    ("outgoing", 1, 256, False, "tail", torch.bfloat16),
+    ("outgoing", 2, 128, True, "pad", torch.bfloat16),
+]
+
+
+@needs_gpu
+@pytest.mark.parametrize("mode,B,N,residual,mkind,dt", CASES)
+def test_native_matches_oracle(mode, B, N, residual, mkind, dt):
+    m = make_layer(mode, residual).cuda()
+    gen = torch.Generator().manual_seed(1)
+    z = torch.randn(B, N, N, 128, generator=gen).to(dt)
+    mask = make_mask(mkind, B, N, gen)
+    ref = oracle_out(m, z, mask)
+    out = _native(m, z.cuda(), None if mask is None else mask.cuda())
+    assert out.dtype == torch.float32 and out.shape == z.shape
+    max_abs, mean_rel = compare(out, ref)
+    assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (max_abs, mean_rel)
+
+
+@needs_gpu
+@pytest.mark.parametrize("mode", ["outgoing", "incoming"])
+def test_native_c3_shape(mode):
+    """Config C3: B=2, N=512, z*0.5, padding masks with lengths in [384, 512]."""
+    m = make_layer(mode, True).cuda()
+    gen = torch.Generator().manual_seed(3)
+    z = (0.5 * torch.randn(2, 512, 512, 128, generator=gen)).to(torch.bfloat16)
+    r = torch.zeros(2, 512)
+    for b in range(2):
+        r[b, :int(torch.randint(384, 513, (1,), generator=gen))] = 1
+    mask = r[:, :, None] * r[:, None, :]
+    ref = oracle_out(m, z, mask)
+    out = _native(m, z.cuda(), mask.cuda())
+    max_abs, mean_rel = compare(out, ref)
+    assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (max_abs, mean_rel)
+
+
+@needs_gpu
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+def test_half_outputs(out_dtype):
+    m = make_layer("outgoing", True).cuda()
+    z = torch.randn(1, 96, 96, 128, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    ref = oracle_out(m, z, None)
+    out = _native(m, z.cuda(), None, out_dtype=out_dtype)
+    assert out.dtype == out_dtype
+    max_abs, mean_rel = compare(out, ref)
+    assert max_abs <= MAX_ABS and mean_rel <= 4e-3, (max_abs, mean_rel)
+
+
+@needs_gpu
+def test_golden_fixtures_d128():
+    """The fixtures made by running the reference itself (tests/golden/)."""
+    import glob
+    import os
+    from tests.test_oracle_golden import load_fixture
+    files = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*d128*.npz")))
+    assert files
+    for f in files:
+        fx = load_fixture(f)
+        m = make_layer(fx["mode"], fx["residual"], ln_noise=False)
+        m._impl.load_state_dict({k: torch.from_numpy(v) for k, v in fx["params"].items()})
+        m = m.cuda()
+        z = torch.from_numpy(fx["z"]).to(fx["z_dtype"])
+        mask = None if fx["mask"] is None else torch.from_numpy(fx["mask"]).cuda()
+        out = _native(m, z.cuda(), mask)
+        max_abs, mean_rel = compare(out, fx["out_ref_fp32"].astype(np.float64))
+        assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (f, max_abs, mean_rel)
+
+
+@needs_gpu
+@pytest.mark.parametrize("L,m,n,k", [(3, 64, 64, 64), (2, 200, 136, 72), (4, 256, 512, 1024),
+                                     (1, 1024, 1024, 1024), (2, 8, 8, 8)])
+def test_contraction_vs_matmul(L, m, n, k):
+    """ftm_contraction alone against an fp32 matmul of the same fp16 operands."""
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    A = torch.randn(L, m, k, device="cuda", generator=g).half()
+    B = torch.randn(L, n, k, device="cuda", generator=g).half()
+    X = torch.full((L, m, n), float("nan"), device="cuda", dtype=torch.half)
+    err = torch.zeros(64, dtype=torch.int32, device="cuda")
+    st = lib.ftm_contraction(A.data_ptr(), B.data_ptr(), X.data_ptr(), L, m, k, n, 1,
+                             err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0, _lib.status_string(st)
+    assert lib.ftm_check_error(err.data_ptr(), None, torch.cuda.current_stream().cuda_stream) == 0
+    ref = torch.bmm(A.float(), B.float().transpose(1, 2))
+    assert torch.isfinite(X).all()
+    rel = ((X.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 2e-3, rel
+
+
+@needs_gpu
+def test_contraction_blocked_b():
+    """B given as row blocks (the layout an all-gather of row shards produces)."""
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    L, m, k, rpb, blocks = 3, 256, 512, 256, 2
+    g = torch.Generator(device="cuda").manual_seed(8)
+    A = torch.randn(L, m, k, device="cuda", generator=g).half()
+    Bb = torch.randn(blocks, L, rpb, k, device="cuda", generator=g).half()
+    X = torch.empty(L, m, rpb * blocks, device="cuda", dtype=torch.half)
+    err = torch.zeros(64, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.ftm_contraction(A.data_ptr(), Bb.data_ptr(), X.data_ptr(), L, m, k, rpb, blocks,
+                               err.data_ptr(), s) == 0
+    assert lib.ftm_check_error(err.data_ptr(), None, s) == 0
+    Bfull = Bb.permute(1, 0, 2, 3).reshape(L, blocks * rpb, k)
+    ref = torch.bmm(A.float(), Bfull.float().transpose(1, 2))
+    rel = ((X.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 2e-3, rel
+
+
+@needs_gpu
+def test_output_canaries_and_error_word():
+    """Writes stay inside `out` (guard regions untouched) and no wait timed out."""
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    m = make_layer("incoming", True).cuda()
+    N, guard = 40, 4096
+    z = torch.randn(1, N, N, 128, device="cuda").half()
+    buf = torch.full((guard * 2 + z.numel(),), 7.0, device="cuda", dtype=torch.float32)
+    out = buf[guard:guard + z.numel()].view(z.shape)
+    packed, _ = m._impl.packed_params()
+    prob = m._impl.problem(z, torch.float32)
+    nbytes = lib.ftm_workspace_bytes(prob)
+    ws = torch.empty(nbytes + 512, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    st = lib.ftm_trimul_fwd(prob, z.data_ptr(), None, packed.data_ptr(), out.data_ptr(),
+                            ws.data_ptr(), nbytes, s)
+    assert st == 0
+    detail = __import__("ctypes").c_int(0)
+    assert lib.ftm_check_error(lib.ftm_workspace_error_word(prob, ws.data_ptr()),
+                               __import__("ctypes").byref(detail), s) == 0, detail.value
+    assert (buf[:guard] == 7.0).all() and (buf[-guard:] == 7.0).all()
+    assert torch.isfinite(out).all()
+
+
+@needs_gpu
+def test_bad_arguments_return_status():
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    m = make_layer("outgoing", True).cuda()
+    z = torch.randn(1, 12, 12, 128, device="cuda").half()     # N % 8 != 0
+    prob = m._impl.problem(z, torch.float32)
+    assert lib.ftm_workspace_bytes(prob) == 0
+    assert lib.ftm_trimul_fwd(prob, z.data_ptr(), None, z.data_ptr(), z.data_ptr(),
+                              z.data_ptr(), 0, None) == _lib.BAD_SHAPE

@@ -1,0 +1,379 @@
+"""Benchmark of the TriMul forward on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Workload: one outgoing TriMul, B=1, N=2048, c_z=c_h=128,
+bf16 z ~ N(0,1), all-ones pair mask, random-init weights. One step = one forward.
+N=1 runs it on one GPU; N>1 shards the i-rows over N ranks with an NCCL all-gather
+of b (fast_trimul_b200.distributed), so total work is fixed ("scaling": "strong").
+
+Metric: TFLOP/s by the reference's FLOP formula (fast_trimul/benchmark.py:77-83)
+over the device time of K steps (CUDA events, barrier + synchronize on both sides,
+max over ranks). z (1.07 GB) is larger than L2, so no flush is needed between steps.
+`e2e` is the same metric through the public module API with the input copied from
+pinned host memory and the output copied back inside the timed region.
+
+`--impl reference` times the reference algorithm's CPU path (the numpy port in
+oracle/, all host threads) on a bounded sample of the same workload.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+C = 128
+N_DEFAULT = 2048
+MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# DRAM traffic per launch from one ncu capture of each kernel (bytes read + written),
+# scaled to N=2048 by positions processed; see profiles/ for the captures.
+NCU_TRAFFIC_N2048 = {"contraction": None, "input_stage": None, "output_stage": None}
+
+
+def trimul_flops(batch, n, c_z=C, c_h=C):
+    m = batch * n * n
+    return 4 * 2 * m * c_z * c_h + 2 * m * c_z * c_z + 2 * m * c_h * c_z + 2 * batch * c_h * n ** 3
+
+
+def stage_model(batch, n, rows=None, world=1):
+    """Algorithmic FLOPs and bytes per launch of each kernel (rows = local i-rows)."""
+    rows = n if rows is None else rows
+    pos = batch * rows * n
+    return {
+        # read z (2c) + mask (4), write a and b (2 * 2c) per position
+        "input_stage": {"flops": 2 * pos * C * 4 * C, "bytes": pos * (2 * C + 4 + 4 * C)},
+        # read a (local rows) and b (all rows), write x
+        "contraction": {"flops": 2 * batch * C * rows * n * n,
+                        "bytes": 2 * batch * C * (rows * n + n * n + rows * n)},
+        # read z, mask, x; write out (bf16)
+        "output_stage": {"flops": 2 * pos * C * 2 * C, "bytes": pos * (2 * C + 4 + 2 * C + 2 * C)},
+    }
+
+
+def load_peaks():
+    try:
+        with open(MEASURED_PEAKS) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        loaded = [x for x in sm if x > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- reference
+def cpu_sample_forward(n=512, seed=0):
+    """One outgoing forward of the workload at a bounded size on the CPU oracle."""
+    import numpy as np
+    from oracle.trimul_oracle import trimul_forward
+    rng = np.random.default_rng(seed)
+    p = {}
+    for ln in ("norm_in", "norm_out"):
+        p[ln + ".weight"] = np.ones(C, np.float32)
+        p[ln + ".bias"] = np.zeros(C, np.float32)
+    for lin in ("proj_a", "gate_a", "proj_b", "gate_b", "proj_g", "proj_out"):
+        bound = C ** -0.5
+        p[lin + ".weight"] = rng.uniform(-bound, bound, (C, C)).astype(np.float32)
+        p[lin + ".bias"] = rng.uniform(-bound, bound, C).astype(np.float32)
+    z = rng.standard_normal((1, n, n, C)).astype(np.float32)
+    mask = np.ones((1, n, n), np.float32)
+    return lambda: trimul_forward(z, p, "outgoing", True, mask)
+
+
+def time_cpu(steps, warmup, n=512, budget_s=None):
+    fn = cpu_sample_forward(n)
+    for _ in range(warmup):
+        fn()
+    ts = []
+    t_end = None if budget_s is None else time.perf_counter() + budget_s
+    while len(ts) < steps or (t_end is not None and time.perf_counter() < t_end and len(ts) < 1000):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return ts
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        return max([i.get("num_threads", 1) for i in info] or [os.cpu_count()])
+    except Exception:
+        return os.cpu_count()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    n_sample = 256
+    ts = time_cpu(args.steps, args.warmup, n_sample)
+    sec = sum(ts) / len(ts)
+    tflops = trimul_flops(1, n_sample) / sec / 1e12
+    cores = cpu_threads()
+    sample = (f"one outgoing forward at N={n_sample} (B=1, c_z=c_h=128, ones mask) per step, "
+              f"fp32 numpy port of the reference's torch path, {cores} threads; "
+              f"TFLOP/s by the reference formula")
+    line = {
+        "metric": "trimul_fwd_tflops", "value": round(tflops, 5), "unit": "TFLOP/s",
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C5 outgoing TriMul B=1 N=2048 c=128 (CPU sample N=256)",
+                   "batch": 1, "n": N_DEFAULT, "c_z": C, "c_h": C, "mode": "outgoing"},
+        "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOP/s", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(tflops, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- ours, 1 GPU
+def make_layer(device):
+    import torch
+    from fast_trimul_b200 import FastTriangleMultiplication
+    torch.manual_seed(0)
+    return FastTriangleMultiplication(C, C, mode="outgoing", residual=True).to(device).eval()
+
+
+def bench_single(args, torch):
+    from fast_trimul_b200.plan import TriMulPlan
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = args.n
+    layer = make_layer(dev)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    z = torch.randn(1, n, n, C, device=dev, generator=gen).to(torch.bfloat16)
+    mask = torch.ones(1, n, n, device=dev)
+    plan = TriMulPlan(layer._impl, 1, n, torch.bfloat16)
+    out = plan.out_like()
+    for _ in range(args.warmup):
+        plan(z, mask, out=out)
+    plan.check_error()
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        t0.record()
+        for k in range(K):
+            plan(z, mask, out=out, stage_events=evs[k])
+        t1.record()
+        torch.cuda.synchronize()
+    plan.check_error()
+    total_ms = t0.elapsed_time(t1)
+    stage_ms = {
+        "input_stage": sum(e[0].elapsed_time(e[1]) for e in evs) / K,
+        "contraction": sum(e[1].elapsed_time(e[2]) for e in evs) / K,
+        "output_stage": sum(e[2].elapsed_time(e[3]) for e in evs) / K,
+    }
+    res = {"ms_per_step": total_ms / K, "stage_ms": stage_ms, "clocks": clk.summary(),
+           "gpu_launches": 3 * K}
+    res["e2e"] = bench_e2e(args, torch, layer, dev, n)
+    res["sweep"] = bench_sweep(args, torch, layer, dev) if not args.no_sweep else None
+    return res
+
+
+def bench_e2e(args, torch, layer, dev, n):
+    """Public API (module forward), pinned host input copied in and output copied out."""
+    gen = torch.Generator().manual_seed(2)
+    z_host = torch.randn(1, n, n, C, generator=gen).to(torch.bfloat16).pin_memory()
+    mask_host = torch.ones(1, n, n).pin_memory()
+    out_host = torch.empty_like(z_host).pin_memory()
+    steps = max(3, min(args.steps, 20))
+
+    def step():
+        zd = z_host.to(dev, non_blocking=True)
+        md = mask_host.to(dev, non_blocking=True)
+        with torch.no_grad():
+            o = layer(zd, mask=md)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    return {"value": round(trimul_flops(1, n) / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 3), "steps": steps,
+            "h2d_bytes_per_step": z_host.numel() * 2 + mask_host.numel() * 4,
+            "d2h_bytes_per_step": out_host.numel() * 2}
+
+
+def bench_sweep(args, torch, layer, dev):
+    """Latency / TFLOP/s at the other sizes the metric names (median of per-step events)."""
+    from fast_trimul_b200.plan import TriMulPlan
+    rows = []
+    for n, mode in ((256, "outgoing"), (256, "incoming"), (512, "outgoing"), (1024, "outgoing"),
+                    (1024, "incoming"), (2048, "incoming")):
+        layer._impl.mode = mode
+        z = torch.randn(1, n, n, C, device=dev).to(torch.bfloat16)
+        mask = torch.ones(1, n, n, device=dev)
+        plan = TriMulPlan(layer._impl, 1, n, torch.bfloat16)
+        out = plan.out_like()
+        for _ in range(5):
+            plan(z, mask, out=out)
+        ts = []
+        for _ in range(20):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            plan(z, mask, out=out)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        plan.check_error()
+        ms = statistics.median(ts)
+        rows.append({"n": n, "mode": mode, "ms": round(ms, 4),
+                     "tflops": round(trimul_flops(1, n) / (ms * 1e-3) / 1e12, 2)})
+        del plan, z, out
+    layer._impl.mode = "outgoing"
+    return rows
+
+
+# --------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=N_DEFAULT)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        from fast_trimul_b200.distributed import bench_sharded
+        res = bench_sharded(args, torch)
+        if res is None:      # non-zero ranks
+            return
+    else:
+        res = bench_single(args, torch)
+
+    n = args.n
+    flops = trimul_flops(1, n)
+    ms = res["ms_per_step"]
+    peaks, peak_src = load_peaks()
+    model = stage_model(1, n, rows=res.get("rows_per_rank"), world=world)
+    dom = "contraction"
+    dom_ms = res["stage_ms"][dom]
+    achieved = model[dom]["flops"] / (dom_ms * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    traffic = NCU_TRAFFIC_N2048.get(dom) if world == 1 and n == N_DEFAULT else None
+    stages = {}
+    for name, st in model.items():
+        t = res["stage_ms"][name] * 1e-3
+        stages[name] = {"ms": round(res["stage_ms"][name], 4),
+                        "tflops": round(st["flops"] / t / 1e12, 1),
+                        "gbs": round(st["bytes"] / t / 1e9, 1),
+                        "tensor_frac": round(st["flops"] / t / 1e12 / peak, 3),
+                        "hbm_frac": round(st["bytes"] / t / 1e9 / float(peaks["hbm_gbs"]), 3)}
+    line = {
+        "metric": "trimul_fwd_tflops", "value": round(flops / (ms * 1e-3) / 1e12, 3),
+        "unit": "TFLOP/s", "n_gpus": max(world, args.gpus), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (z ~ N(0,1) bf16, ones mask, seeded random-init weights)",
+        "config": {"workload": f"C5 outgoing TriMul B=1 N={n} c_z=c_h=128", "batch": 1, "n": n,
+                   "c_z": C, "c_h": C, "mode": "outgoing", "z_dtype": "bf16",
+                   "parallelism": f"i-row shards x{max(world, args.gpus)}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (z = %.2f GB)" % (n * n * C * 2 / 1e9)},
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 3),
+                     "peak_source": f"{peak_src} bf16 dense burst (MEASURED_PEAKS.json)",
+                     "traffic": traffic, "algorithmic_bytes": model[dom]["bytes"]},
+        "stages": stages,
+        "clocks": res["clocks"],
+        "e2e": res.get("e2e"),
+        "gpu_launches": res["gpu_launches"],
+    }
+    if res.get("sweep"):
+        line["sweep"] = res["sweep"]
+    if res.get("comm"):
+        line["comm"] = res["comm"]
+    if world == 1 and not args.no_cpu_baseline:
+        ts = time_cpu(2, 1, 256, budget_s=10.0)
+        sec = statistics.median(ts)
+        line["cpu_baseline"] = {
+            "value": round(trimul_flops(1, 256) / sec / 1e12, 5), "unit": "TFLOP/s",
+            "cores": cpu_threads(), "kind": "port",
+            "sample": f"oracle (numpy fp32 port of the reference's torch path) on one outgoing "
+                      f"N=256 forward, median of {len(ts)} runs (~10 s), all host threads"}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -247,7 +247,9 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t row, uint32_t chunk) {
 }
 
 // -------------------------------------------------------------- small math
-__device__ __forceinline__ float sigmoidf_fast(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// logistic function with the fast exp2-based exponential and approximate divide
+// (relative error ~1e-7, far below the fp16 storage rounding that follows)
+__device__ __forceinline__ float sigmoidf_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);

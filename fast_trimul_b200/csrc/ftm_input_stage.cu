@@ -10,12 +10,16 @@
 //               fp16, 128 KB) is loaded once and stays resident.
 //   warps 2-5   per row: fp32 mean/variance of z*mask (the LayerNorm statistics),
 //               bf16 -> fp16 in place when z is bf16, then mark the slot ready.
-//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) x 8 per half into
-//               TMEM: half 0 = [a_p | a_g] (256 columns), half 1 = [b_p | b_g].
-//   warps 6-9   TMEM -> registers; proj = m*rstd*(acc - mean*rowsum(W')) + (W beta + b);
-//               a = proj_p * sigmoid(proj_g); fp16 stores to a_cm[b][c][u][v].
-// The two TMEM halves are separate 256-column slots, so the MMA of tile t+1's a-half
-// overlaps the epilogue of tile t's b-half.
+//   warp 1      one thread issues tcgen05.mma with the WEIGHT as the A operand and the
+//               z tile as B (M = 128 channels, N = 128 positions, K = 16) so TMEM lanes
+//               are channels and columns are positions: slot 0 = [a_p | a_g], slot 1 =
+//               [b_p | b_g], 256 columns each.
+//   warps 6-13  TMEM -> registers (lane = channel, 32 positions per load);
+//               proj = m*rstd*(acc - mean*rowsum(W')) + (W beta + b),
+//               a = proj_p * sigmoid(proj_g); each thread stores 64 contiguous bytes of
+//               its channel plane a_cm[b][c][u][v] (16-byte stores).
+// The two TMEM slots are independent, so the MMA of tile t+1's a-slot overlaps the
+// epilogue of tile t's b-slot.
 #include "ftm_kernels.h"
 
 namespace ftm {
@@ -65,11 +69,11 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     for (int s = 0; s < kInBufs; ++s) {
       mbar_init(&z_full[s], 1);
       mbar_init(&a_ready[s], 128);
-      mbar_init(&buf_empty[s], 1 + 4);  // MMA commit + 4 epilogue warps (stats read)
+      mbar_init(&buf_empty[s], 1 + 8);  // MMA commit + 8 epilogue warps (stats read)
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&tmem_full[h], 1);
-      mbar_init(&tmem_empty[h], 4);
+      mbar_init(&tmem_empty[h], 8);
     }
     mbar_init(mma_drain, 1);
     fence_mbar_init();
@@ -116,7 +120,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(0, 128, 256, 0, 0);
+      constexpr uint32_t idesc = idesc_f16(0, 128, 128, 0, 0);
       const uint32_t wbase = smem_u32(sW);
       const uint32_t zbase = smem_u32(sZ);
       bool ok = mbar_wait(w_full, 0, err, err_code(KERNEL_INPUT, ROLE_MMA, 1));
@@ -129,19 +133,24 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           break;
         }
         tc_fence_after();
-        const uint32_t abase = zbase + s * kZTile;
+        const uint32_t zb = zbase + s * kZTile;
         for (int h = 0; h < 2; ++h) {
           if (!mbar_wait(&tmem_empty[h], (it & 1) ^ 1, err, err_code(KERNEL_INPUT, ROLE_MMA, 3))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t d = tmem_base + h * 256;
+          // D[channel][position] = W'[2h+g] (128 ch x 128 k) * z^T; g = 0 proj, 1 gate
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = kmajor_desc(abase + (kk >> 2) * (kZTile / 2) + (kk & 3) * 32);
-            const uint64_t bd = kmajor_desc(wbase + (kk >> 2) * 65536 + h * 32768 + (kk & 3) * 32);
-            umma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          for (int g = 0; g < 2; ++g) {
+            const uint32_t d = tmem_base + h * 256 + g * 128;
+            const uint32_t wg = wbase + (2 * h + g) * 16384;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t ad = kmajor_desc(wg + (kk >> 2) * 65536 + (kk & 3) * 32);
+              const uint64_t bd = kmajor_desc(zb + (kk >> 2) * (kZTile / 2) + (kk & 3) * 32);
+              umma_f16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+            }
           }
           umma_commit(&tmem_full[h]);
         }
@@ -228,40 +237,58 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     }
   } else {
     // ----------------------------------------------------------------- epilogue
-    const int sub = warp & 3;
-    const int row = sub * 32 + lane;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(sub * 32) << 16);
+    // warp -> (TMEM lane quarter = 32 channels, half of the tile's 128 positions)
+    const int ew = warp - 6;
+    const int quarter = warp & 3;
+    const int phalf = ew >> 2;
+    const int c = quarter * 32 + lane;                 // this thread's channel
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    float up[2], vp[2], ug[2], vg[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      up[h] = sU[h * 256 + c];
+      vp[h] = sV[h * 256 + c];
+      ug[h] = sU[h * 256 + 128 + c];
+      vg[h] = sV[h * 256 + 128 + c];
+    }
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
       const int s = it % kInBufs;
       int b, u0, v0;
       tl.tile(t, b, u0, v0);
-      const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
-      const bool valid = (u < tl.R) && (v < tl.S);
-      const size_t pos = static_cast<size_t>(u) * tl.S + v;
       if (!mbar_wait_warp(&a_ready[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_EPILOGUE, 1))) break;
-      const float2 st = sStats[s * 128 + row];
+      const float2* st = sStats + s * 128;
       for (int h = 0; h < 2; ++h) {
         if (!mbar_wait_warp(&tmem_full[h], it & 1, err, err_code(KERNEL_INPUT, ROLE_EPILOGUE, 2))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        __half* dst = (h == 0 ? a_cm : b_cm) + static_cast<size_t>(b) * kC * plane + pos;
-        const float* up = sU + h * 256;
-        const float* vp = sV + h * 256;
+        __half* plane_c = (h == 0 ? a_cm : b_cm) + (static_cast<size_t>(b) * kC + c) * plane;
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int j = 0; j < 2; ++j) {
+          const int p0 = phalf * 64 + j * 32;        // first tile row of this chunk
+          const int u = u0 + p0 / tl.vt, v = v0 + p0 % tl.vt;
           float p[32], g[32];
-          tmem_ld32(lane_base + h * 256 + cb * 32, p);
-          tmem_ld32(lane_base + h * 256 + 128 + cb * 32, g);
+          tmem_ld32(lane_base + h * 256 + p0, p);
+          tmem_ld32(lane_base + h * 256 + 128 + p0, g);
+          uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = cb * 32 + i;
-            const float pv = fmaf(st.x, p[i], fmaf(st.y, up[c], vp[c]));
-            const float gv = fmaf(st.x, g[i], fmaf(st.y, up[128 + c], vp[128 + c]));
-            if (valid) dst[static_cast<size_t>(c) * plane] = __float2half_rn(pv * sigmoidf_fast(gv));
+          for (int i = 0; i < 32; i += 2) {
+            const float2 s0 = st[p0 + i], s1 = st[p0 + i + 1];
+            const float pv0 = fmaf(s0.x, p[i], fmaf(s0.y, up[h], vp[h]));
+            const float gv0 = fmaf(s0.x, g[i], fmaf(s0.y, ug[h], vg[h]));
+            const float pv1 = fmaf(s1.x, p[i + 1], fmaf(s1.y, up[h], vp[h]));
+            const float gv1 = fmaf(s1.x, g[i + 1], fmaf(s1.y, ug[h], vg[h]));
+            packed[i / 2] = pack_half2(pv0 * sigmoidf_fast(gv0), pv1 * sigmoidf_fast(gv1));
+          }
+          if (u < tl.R) {
+            uint4* dst = reinterpret_cast<uint4*>(plane_c + static_cast<size_t>(u) * tl.S + v);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (v + 8 * q < tl.S)
+                dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
           }
         }
         tc_fence_before();

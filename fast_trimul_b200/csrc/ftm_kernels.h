@@ -30,9 +30,9 @@ struct PackedLayout {
 };
 
 constexpr int kC = 128;            // c_z == c_h supported by the tensor-core kernels
-constexpr int kInThreads = 320;    // producer, MMA, 4 transform, 4 epilogue warps
+constexpr int kInThreads = 448;    // producer, MMA, 4 transform, 8 epilogue warps
 constexpr int kInBufs = 2;
-constexpr int kOutThreads = 320;
+constexpr int kOutThreads = 448;   // producer, MMA, 4 transform, 8 epilogue warps
 constexpr int kOutBufs = 2;
 constexpr int kCtThreads = 192;    // producer, MMA, 4 epilogue warps
 constexpr int kCtStages = 4;

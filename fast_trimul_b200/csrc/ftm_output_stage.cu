@@ -13,7 +13,9 @@
 //              of z in place when needed.
 //   warp 1     tcgen05.mma: TMEM[0:128) = z W_g'^T (K-major A), TMEM[128:256) =
 //              x W_o'^T (MN-major A); two 256-column accumulators alternate tiles.
-//   warps 6-9  epilogue: fold the statistics back in, gate, residual, mask, store.
+//   warps 6-13 epilogue (two warps per TMEM lane quarter, each owning half of the
+//              128 output channels): fold the statistics back in, gate, residual,
+//              mask, store.
 #include "ftm_kernels.h"
 
 namespace ftm {
@@ -100,11 +102,11 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     for (int s = 0; s < kOutBufs; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&a_ready[s], 128);
-      mbar_init(&buf_empty[s], 4);  // epilogue warps (they finish after the MMA read)
+      mbar_init(&buf_empty[s], 8);  // epilogue warps (they finish after the MMA read)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4);
+      mbar_init(&tmem_empty[a], 8);
     }
     mbar_init(mma_drain, 1);
     fence_mbar_init();
@@ -273,6 +275,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     }
   } else {
     const int sub = warp & 3;
+    const int nhalf = (warp - 6) >> 2;   // output channels [64 * nhalf, 64 * nhalf + 64)
     const int row = sub * 32 + lane;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(sub * 32) << 16);
     int it = 0;
@@ -292,7 +295,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const float m = sMask[s * 128 + row];
       const uint8_t* zs = sSlots + s * kSlot;
 #pragma unroll 1
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 2 * nhalf; cb < 2 * nhalf + 2; ++cb) {
         float ga[32], oa[32];
         tmem_ld32(lane_base + s * 256 + cb * 32, ga);
         tmem_ld32(lane_base + s * 256 + 128 + cb * 32, oa);

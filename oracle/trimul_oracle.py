@@ -45,7 +45,11 @@ def sigmoid(x):
 
 
 def linear(x, w, b):
-    return x @ w.T + b
+    """x @ w^T + b over the last dim (as a single 2-D BLAS call)."""
+    lead = x.shape[:-1]
+    y = x.reshape(-1, x.shape[-1]) @ w.T
+    y += b
+    return y.reshape(*lead, w.shape[0])
 
 
 def contract(a, b, mode):

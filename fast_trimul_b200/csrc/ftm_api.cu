@@ -48,9 +48,11 @@ bool arch_ok(int* dev_out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// 128B-swizzled tiled map over `rank` dims; strides in bytes for dims 1..rank-1
+// tiled map over `rank` dims (128B swizzle unless told otherwise); strides in bytes
+// for dims 1..rank-1
 bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base,
-              const uint64_t* dims, const uint64_t* strides, const uint32_t* box) {
+              const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+              CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t d[5], s[4];
@@ -63,7 +65,7 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base
   for (int i = 0; i < rank - 1; ++i) s[i] = strides[i];
   const CUresult r =
       fn(m, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -121,9 +123,22 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
     if (!make_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pk + L.w_in, dims, strides, box))
       return FTM_LAUNCH_FAILED;
   }
+  // channel-major outputs (S, R, C, B): stores of [32 channel x 32 position] blocks
+  CUtensorMap amap, bmap;
+  {
+    const uint64_t R = p->rows, S = p->cols;
+    const uint64_t dims[4] = {S, R, uint64_t(kC), uint64_t(p->batch)};
+    const uint64_t strides[3] = {S * 2, R * S * 2, uint64_t(kC) * R * S * 2};
+    const uint32_t box[4] = {32, 1, 32, 1};
+    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, a_cm, dims, strides, box,
+                  CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, b_cm, dims, strides, box,
+                  CU_TENSOR_MAP_SWIZZLE_64B))
+      return FTM_LAUNCH_FAILED;
+  }
   const int grid = tl.tiles < sm_count(dev) ? tl.tiles : sm_count(dev);
   cudaError_t e = launch_input_stage(
-      zmap, wmap, mask, reinterpret_cast<const float*>(pk + L.u_in),
+      zmap, wmap, amap, bmap, mask, reinterpret_cast<const float*>(pk + L.u_in),
       reinterpret_cast<const float*>(pk + L.v_in), static_cast<__half*>(a_cm),
       static_cast<__half*>(b_cm), tl, incoming ? 1 : 0, p->z_dtype == FTM_BF16 ? 1 : 0,
       p->eps_in, err, grid, stream);
@@ -179,8 +194,18 @@ int stage_out(const ftm_problem* p, const void* z, const float* mask, const void
       return FTM_LAUNCH_FAILED;
   }
   const int grid = tl.tiles < sm_count(dev) ? tl.tiles : sm_count(dev);
+  // out (16-bit) written like z: (C, S, R, B), 32 positions x 64 channels per store
+  CUtensorMap omap = zmap;
+  if (p->out_dtype != FTM_F32) {
+    const uint64_t C = kC, R = p->rows, S = p->cols, B = p->batch;
+    const uint64_t dims[4] = {C, S, R, B};
+    const uint64_t strides[3] = {C * 2, S * C * 2, R * S * C * 2};
+    const uint32_t box[4] = {64, 32, 1, 1};
+    if (!make_map(&omap, tma_dtype(p->out_dtype), 4, out, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
   cudaError_t e = launch_output_stage(
-      zmap, xmap, wmap, mask, reinterpret_cast<const float*>(pk + L.u_g),
+      zmap, xmap, wmap, omap, mask, reinterpret_cast<const float*>(pk + L.u_g),
       reinterpret_cast<const float*>(pk + L.v_g), reinterpret_cast<const float*>(pk + L.u_o),
       reinterpret_cast<const float*>(pk + L.v_o), out, p->out_dtype, tl, p->residual ? 1 : 0,
       p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, p->eps_out, err, grid, stream);

@@ -16,8 +16,9 @@
 //               [b_p | b_g], 256 columns each.
 //   warps 6-13  TMEM -> registers (lane = channel, 32 positions per load);
 //               proj = m*rstd*(acc - mean*rowsum(W')) + (W beta + b),
-//               a = proj_p * sigmoid(proj_g); each thread stores 64 contiguous bytes of
-//               its channel plane a_cm[b][c][u][v] (16-byte stores).
+//               a = proj_p * sigmoid(proj_g); each warp stages a [32 channel x 32
+//               position] block in shared memory and TMA-stores it into the channel
+//               planes a_cm[b][c][u][v].
 // The two TMEM slots are independent, so the MMA of tile t+1's a-slot overlaps the
 // epilogue of tile t's b-slot.
 #include "ftm_kernels.h"
@@ -31,15 +32,18 @@ constexpr int kWBytes = 4 * kC * kC * 2;      // 128 KB
 constexpr int kOffW = 0;
 constexpr int kOffZ = kOffW + kWBytes;
 constexpr int kOffStats = kOffZ + kInBufs * kZTile;
-constexpr int kOffUV = kOffStats + kInBufs * 128 * 8;
-constexpr int kOffBar = kOffUV + 2 * 4 * kC * 4;
+constexpr int kStageBytes = 32 * 32 * 2;       // one warp's 32 channels x 32 positions
+constexpr int kOffStage = ((kOffStats + kInBufs * 128 * 8) + 1023) & ~1023;
+constexpr int kOffBar = kOffStage + 8 * kStageBytes;
 constexpr int kNumBars = 1 + 3 * kInBufs + 4 + 1;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmem + 16 + 1024;  // + alignment slack
 
 __global__ void __launch_bounds__(kInThreads, 1)
 input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
-                   const __grid_constant__ CUtensorMap wmap, const float* __restrict__ mask,
+                   const __grid_constant__ CUtensorMap wmap,
+                   const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap bmap, const float* __restrict__ mask,
                    const float* __restrict__ u_in, const float* __restrict__ v_in,
                    __half* __restrict__ a_cm, __half* __restrict__ b_cm, PosTiling tl,
                    int incoming, int z_bf16, float eps, int* err) {
@@ -49,8 +53,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   uint8_t* sW = smem + kOffW;
   uint8_t* sZ = smem + kOffZ;
   float2* sStats = reinterpret_cast<float2*>(smem + kOffStats);
-  float* sU = reinterpret_cast<float*>(smem + kOffUV);
-  float* sV = sU + 4 * kC;
+  uint8_t* sStage = smem + kOffStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_full = bars;
   uint64_t* z_full = bars + 1;
@@ -78,10 +81,6 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 4 * kC; i += blockDim.x) {
-    sU[i] = u_in[i];
-    sV[i] = v_in[i];
-  }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -89,7 +88,6 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   const uint32_t tmem_base = *tmem_slot;
 
   const int ntiles = tl.tiles;
-  const size_t plane = static_cast<size_t>(tl.R) * tl.S;  // positions per (batch, channel)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -246,11 +244,12 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     float up[2], vp[2], ug[2], vg[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      up[h] = sU[h * 256 + c];
-      vp[h] = sV[h * 256 + c];
-      ug[h] = sU[h * 256 + 128 + c];
-      vg[h] = sV[h * 256 + 128 + c];
+      up[h] = __ldg(u_in + h * 256 + c);
+      vp[h] = __ldg(v_in + h * 256 + c);
+      ug[h] = __ldg(u_in + h * 256 + 128 + c);
+      vg[h] = __ldg(v_in + h * 256 + 128 + c);
     }
+    uint8_t* stage = sStage + ew * kStageBytes;
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
@@ -265,7 +264,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           break;
         }
         tc_fence_after();
-        __half* plane_c = (h == 0 ? a_cm : b_cm) + (static_cast<size_t>(b) * kC + c) * plane;
+        const CUtensorMap* omap = h == 0 ? &amap : &bmap;
 #pragma unroll 1
         for (int j = 0; j < 2; ++j) {
           const int p0 = phalf * 64 + j * 32;        // first tile row of this chunk
@@ -283,12 +282,19 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
             const float gv1 = fmaf(s1.x, g[i + 1], fmaf(s1.y, ug[h], vg[h]));
             packed[i / 2] = pack_half2(pv0 * sigmoidf_fast(gv0), pv1 * sigmoidf_fast(gv1));
           }
-          if (u < tl.R) {
-            uint4* dst = reinterpret_cast<uint4*>(plane_c + static_cast<size_t>(u) * tl.S + v);
+          // stage [32 channels][32 positions] (64-byte swizzle) and TMA-store it into
+          // the channel planes; the previous store must have finished reading first
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (v + 8 * q < tl.S)
-                dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(stage + sw64_off(lane, q)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && u < tl.R && v < tl.S) {
+            tma_store_4d(omap, stage, v, u, quarter * 32, b);
+            bulk_commit();
           }
         }
         tc_fence_before();
@@ -298,6 +304,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(&buf_empty[s]);
     }
+    if (lane == 0) bulk_wait0();  // stores complete before the kernel ends
   }
 
   tc_fence_before();
@@ -312,15 +319,17 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
 
 size_t input_stage_smem_bytes() { return kSmemBytes; }
 
-cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap, const float* mask,
+cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
+                               const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
                                const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
                                const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
                                int grid, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, mask, u_in, v_in, a_cm,
-                                                               b_cm, tl, incoming, z_bf16, eps, err);
+  input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, amap, bmap, mask, u_in,
+                                                               v_in, a_cm, b_cm, tl, incoming,
+                                                               z_bf16, eps, err);
   return cudaGetLastError();
 }
 

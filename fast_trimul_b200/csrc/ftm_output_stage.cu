@@ -15,7 +15,8 @@
 //              x W_o'^T (MN-major A); two 256-column accumulators alternate tiles.
 //   warps 6-13 epilogue (two warps per TMEM lane quarter, each owning half of the
 //              128 output channels): fold the statistics back in, gate, residual,
-//              mask, store.
+//              mask; 16-bit outputs are written over the z slot in place and
+//              TMA-stored (32 positions x 64 channels per warp), fp32 stored directly.
 #include "ftm_kernels.h"
 
 namespace ftm {
@@ -68,7 +69,8 @@ template <int OUT_DT>
 __global__ void __launch_bounds__(kOutThreads, 1)
 output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                     const __grid_constant__ CUtensorMap xmap,
-                    const __grid_constant__ CUtensorMap wmap, const float* __restrict__ mask,
+                    const __grid_constant__ CUtensorMap wmap,
+                    const __grid_constant__ CUtensorMap omap, const float* __restrict__ mask,
                     const float* __restrict__ u_g, const float* __restrict__ v_g,
                     const float* __restrict__ u_o, const float* __restrict__ v_o,
                     void* __restrict__ out, PosTiling tl, int residual, int z_bf16,
@@ -293,7 +295,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const size_t elem0 = ((static_cast<size_t>(b) * tl.R + u) * tl.S + v) * kC;
       const float4 st = sStats[s * 128 + row];
       const float m = sMask[s * 128 + row];
-      const uint8_t* zs = sSlots + s * kSlot;
+      uint8_t* zs = sSlots + s * kSlot;
 #pragma unroll 1
       for (int cb = 2 * nhalf; cb < 2 * nhalf + 2; ++cb) {
         float ga[32], oa[32];
@@ -322,9 +324,39 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           const float dlt = g * o;
           r[i] = (residual ? fmaf(m, zv[i], dlt) : dlt) * m;
         }
-        if (valid) store_out32<OUT_DT>(out, elem0 + cb * 32, r);
+        if (OUT_DT == 0) {
+          if (valid) store_out32<OUT_DT>(out, elem0 + cb * 32, r);
+        } else {
+          // 16-bit output: overwrite the z chunks just read (same thread, same
+          // addresses) so the slot holds the out tile in the z tile's layout
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = cb * 4 + q;
+            uint4 o;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2)
+              w[e2] = OUT_DT == 1 ? pack_half2(r[q * 8 + 2 * e2], r[q * 8 + 2 * e2 + 1])
+                                  : pack_bf162(r[q * 8 + 2 * e2], r[q * 8 + 2 * e2 + 1]);
+            *reinterpret_cast<uint4*>(zs + (chunk >> 3) * kHalfTile + sw128_off(row, chunk & 7)) = o;
+          }
+        }
       }
       tc_fence_before();
+      if (OUT_DT != 0) {
+        // TMA-store this warp's 32 rows x 64 channels (clipped at the tensor edges)
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int r0 = sub * 32;
+        const int uw = u0 + r0 / tl.vt, vw = v0 + r0 % tl.vt;
+        if (lane == 0) {
+          if (uw < tl.R && vw < tl.S) {
+            tma_store_4d(&omap, zs + nhalf * kHalfTile + r0 * 128, nhalf * 64, vw, uw, b);
+            bulk_commit();
+          }
+          bulk_wait_read0();   // slot may be refilled once the store has read it
+        }
+      }
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&tmem_empty[s]);
@@ -333,6 +365,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     }
   }
 
+  if (OUT_DT != 0 && warp >= 6 && (threadIdx.x & 31) == 0) bulk_wait0();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -346,7 +379,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
 size_t output_stage_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
-                                const CUtensorMap& wmap, const float* mask, const float* u_g,
+                                const CUtensorMap& wmap, const CUtensorMap& omap, const float* mask, const float* u_g,
                                 const float* v_g, const float* u_o, const float* v_o, void* out,
                                 int out_dtype, const PosTiling& tl, int residual, int z_bf16,
                                 float eps_in, float eps_out, int* err, int grid,
@@ -355,7 +388,7 @@ cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kOutThreads, kSmemBytes, stream>>>(zmap, xmap, wmap, mask, u_g, v_g, u_o, v_o, out,
+    kern<<<grid, kOutThreads, kSmemBytes, stream>>>(zmap, xmap, wmap, omap, mask, u_g, v_g, u_o, v_o, out,
                                                     tl, residual, z_bf16, eps_in, eps_out, err);
     return cudaGetLastError();
   };

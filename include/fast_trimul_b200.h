@@ -111,6 +111,20 @@ int ftm_contraction(const void* A, const void* B, void* X, int32_t L, int32_t m,
 int ftm_output_stage(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
                      const void* packed, void* out, int* err_word, ftm_stream_t stream);
 
+/* ---- whole forward with no allocation ---------------------------------------
+ * No counterpart in the reference. For callers that cannot provide a workspace --
+ * hosts with a fixed device-memory budget handed out at start-up, or hosts that may
+ * not call cudaMalloc while running because it can synchronise the device. Same
+ * arguments and results as ftm_trimul_fwd, but a, b, x and the error word live in a
+ * device array built into the library (about 48 MiB, held by each GPU that loads the
+ * library until exit). Problems with batch*rows*cols > FTM_STATIC_SCRATCH_MAX_POSITIONS
+ * return FTM_BAD_WORKSPACE. All calls on a device share that array: calls that overlap
+ * on the GPU race and must be serialised. The first call on each device looks up the
+ * array's device address; make it before any stream capture. Allocates nothing. */
+#define FTM_STATIC_SCRATCH_MAX_POSITIONS 65536
+int ftm_trimul_fwd_static_scratch(const ftm_problem* p, const void* z, const float* mask,
+                                  const void* packed, void* out, ftm_stream_t stream);
+
 /* ---- status -------------------------------------------------------------- */
 /* Synchronise `stream`, read the device error word of a workspace (or any err_word
  * passed to a stage) and clear it: FTM_OK, or FTM_TIMEOUT when a bounded device wait

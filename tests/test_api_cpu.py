@@ -1,0 +1,259 @@
+"""Host-side API, CPU only. Mirrors the reference's own unit tests
+(tests/test_{registry,context,dispatch,decorators,loaders,patch,smoke}.py of fast_trimul)
+against this package's implementation of the same interface."""
+
+import sys
+import types
+
+import pytest
+import torch
+
+import fast_trimul_b200 as ftm
+from fast_trimul_b200.core import dispatch, registry
+from fast_trimul_b200.core.context import BackendCapabilities, NormalizedInput, normalize
+from fast_trimul_b200.core.decorators import accelerate, accelerated, active_backend
+from fast_trimul_b200.core.registry import get_loader
+from fast_trimul_b200.integrations import patch
+from fast_trimul_b200.integrations.loaders import _OPENFOLD_TO_FAST
+from fast_trimul_b200.ops.triangle import FastTriangleMultiplication
+
+
+# ------------------------------------------------------------------ smoke / API
+def test_public_api_exported():
+    for name in ("FastTriangleMultiplication", "accelerate", "accelerated", "verify",
+                 "list_backends", "patch_openfold", "patch_openfold3", "patch_boltz",
+                 "patch_protenix", "functional"):
+        assert hasattr(ftm, name)
+    assert isinstance(ftm.__version__, str) and ftm.__version__
+    assert hasattr(ftm.functional, "triangle_multiplication")
+    assert {"torch", "cuda"} <= set(ftm.list_backends())
+
+
+# ------------------------------------------------------------------ input guard
+def _caps(dtypes, align=1):
+    return BackendCapabilities(dtypes=dtypes, min_align=align)
+
+
+def test_guard_rejects_non_4d_and_misaligned():
+    assert normalize(torch.randn(4, 4), None, _caps({torch.float16})) is None
+    assert normalize(torch.randn(1, 12, 12, 4), None, _caps({torch.float32}, 8)) is None
+    assert normalize(torch.randn(1, 3, 3, 4), None, _caps({torch.float32})) is not None
+
+
+def test_guard_accepts_and_casts():
+    out = normalize(torch.randn(1, 8, 8, 4), None, _caps({torch.float32}, 8))
+    assert isinstance(out, NormalizedInput) and out.shape == (1, 8, 8, 4)
+    assert normalize(torch.randn(1, 8, 8, 4), None, _caps({torch.float16}, 8)).tensor.dtype == torch.float16
+    z = torch.randn(1, 8, 8, 4).half()
+    assert normalize(z, None, _caps({torch.float32}, 8)).tensor.dtype == torch.float32
+    zb = torch.randn(1, 8, 8, 4).bfloat16()
+    assert normalize(zb, None, _caps({torch.float16}, 8)).tensor.dtype == torch.float16
+
+
+def test_guard_makes_contiguous():
+    z = torch.randn(1, 8, 8, 4).transpose(1, 2)
+    m = torch.ones(1, 8, 8).transpose(1, 2)
+    out = normalize(z, m, _caps({torch.float32}, 8))
+    assert out.tensor.is_contiguous() and out.mask.is_contiguous()
+    assert all(isinstance(s, int) for s in out.strides)
+
+
+# ------------------------------------------------------------------ dispatcher
+def test_dispatch_order():
+    cpu, gpu = torch.device("cpu"), torch.device("cuda")
+    assert dispatch._order(cpu, "torch") == ["torch"]
+    assert dispatch._order(cpu, "cuda") == ["cuda", "torch"]
+    assert dispatch._order(cpu, "auto") == ["torch"]
+    assert dispatch._order(gpu, "auto") == ["cuda", "torch"]
+    with accelerated("torch"):
+        assert dispatch._order(gpu, "auto") == ["torch"]
+
+
+def test_dispatch_runs_registered_backend_and_falls_back():
+    marker = object()
+
+    @registry.backend("__ok", dtypes={torch.float32}, min_align=1)
+    class _Ok:
+        def __init__(self, caps):
+            self.caps = caps
+
+        def execute(self, inp, params):
+            return marker
+
+    @registry.backend("__bad", dtypes={torch.float32}, min_align=1)
+    class _Bad:
+        def __init__(self, caps):
+            self.caps = caps
+
+        def execute(self, inp, params):
+            raise ValueError("declines")
+
+    try:
+        assert dispatch.run(torch.randn(1, 8, 8, 4), None, None, prefer="__ok") is marker
+        # a generic failure falls to "torch", which then needs real params
+        layer = FastTriangleMultiplication(4, 4, "outgoing")
+        out = dispatch.run(torch.randn(1, 8, 8, 4), None, layer._impl, prefer="__bad")
+        assert out.shape == (1, 8, 8, 4)
+    finally:
+        registry._BACKENDS.pop("__ok", None)
+        registry._BACKENDS.pop("__bad", None)
+    with pytest.raises(RuntimeError):
+        dispatch.run(torch.randn(2, 2), None, None, prefer="torch")
+
+
+def test_dispatch_does_not_hide_missing_native_library():
+    from fast_trimul_b200 import _lib
+
+    @registry.backend("__missing", dtypes={torch.float32}, min_align=1)
+    class _Missing:
+        def __init__(self, caps):
+            self.caps = caps
+
+        def execute(self, inp, params):
+            raise _lib.NativeLibraryMissing("no .so")
+
+    try:
+        with pytest.raises(_lib.NativeLibraryMissing):
+            dispatch.run(torch.randn(1, 8, 8, 4), None, None, prefer="__missing")
+    finally:
+        registry._BACKENDS.pop("__missing", None)
+
+
+# ------------------------------------------------------------------ decorators
+def test_scoped_backend():
+    assert active_backend() == "auto"
+    with accelerated("cuda"):
+        assert active_backend() == "cuda"
+        with accelerated("torch"):
+            assert active_backend() == "torch"
+        assert active_backend() == "cuda"
+    assert active_backend() == "auto"
+
+    @accelerate(backend="torch")
+    def where():
+        return active_backend()
+
+    @accelerate
+    def where_auto():
+        return active_backend()
+
+    assert where() == "torch" and where_auto() == "auto" and active_backend() == "auto"
+
+
+# ------------------------------------------------------------------ registry / loaders
+def test_registry_roundtrip():
+    @registry.weights_for("__src")
+    def _l(sd):
+        return sd
+
+    try:
+        assert registry.get_loader("__src") is _l
+    finally:
+        registry._LOADERS.pop("__src", None)
+    with pytest.raises(KeyError):
+        registry.get_loader("__nope__")
+    assert registry.get_backend("__nope__") is None
+    for src in ("openfold", "openfold3", "protenix", "boltz", "chai"):
+        assert callable(get_loader(src))
+
+
+def test_openfold_and_protenix_rename():
+    out = get_loader("openfold")({"layer_norm_in.weight": torch.zeros(2),
+                                  "linear_a_p.weight": torch.zeros(2, 2),
+                                  "linear_z.weight": torch.zeros(2, 2)})
+    assert {"norm_in.weight", "proj_a.weight", "proj_out.weight"} <= set(out)
+    assert "gate_a.weight" in get_loader("protenix")({"linear_a_g.weight": torch.zeros(2, 2)})
+    assert _OPENFOLD_TO_FAST["linear_a_p"] == "proj_a"
+    assert get_loader("chai") is get_loader("boltz")
+
+
+def test_boltz_and_openfold3_split():
+    d = 4
+    p_in = torch.arange(2 * d * d).reshape(2 * d, d).float()
+    sd = {"norm_in.weight": torch.zeros(d), "norm_in.bias": torch.zeros(d),
+          "norm_out.weight": torch.zeros(d), "norm_out.bias": torch.zeros(d),
+          "p_in.weight": p_in, "g_in.weight": torch.zeros(2 * d, d),
+          "p_out.weight": torch.zeros(d, d), "g_out.weight": torch.zeros(d, d)}
+    out = get_loader("boltz")(sd)
+    assert torch.equal(out["proj_a.weight"], p_in[:d]) and torch.equal(out["proj_b.weight"], p_in[d:])
+    of3 = {"layer_norm_in.weight": torch.zeros(d), "layer_norm_in.bias": torch.zeros(d),
+           "layer_norm_out.weight": torch.zeros(d), "layer_norm_out.bias": torch.zeros(d),
+           "linear_ab_p.weight": p_in, "linear_ab_g.weight": torch.zeros(2 * d, d),
+           "linear_ab_p.bias": torch.arange(2 * d).float(),
+           "linear_z.weight": torch.zeros(d, d), "linear_g.weight": torch.zeros(d, d)}
+    out = get_loader("openfold3")(of3)
+    assert torch.equal(out["proj_b.weight"], p_in[d:]) and out["proj_b.bias"].shape == (d,)
+    assert "proj_a.weight" in get_loader("openfold3")({"linear_a_p.weight": torch.zeros(2, 2)})
+
+
+def test_load_weights_zeroes_missing_biases_and_rejects_unknown_keys():
+    d = 8
+    m = FastTriangleMultiplication(d, d, "outgoing")
+    sd = {"norm_in.weight": torch.ones(d), "norm_in.bias": torch.zeros(d),
+          "norm_out.weight": torch.ones(d), "norm_out.bias": torch.zeros(d),
+          "p_in.weight": torch.randn(2 * d, d), "g_in.weight": torch.randn(2 * d, d),
+          "p_out.weight": torch.randn(d, d), "g_out.weight": torch.randn(d, d)}
+    m.load_boltz_state_dict(sd)
+    assert torch.all(m._impl.proj_a.bias == 0) and torch.all(m._impl.proj_out.bias == 0)
+    with pytest.raises(KeyError):
+        m.load_weights({"bogus.weight": torch.zeros(1)}, "openfold")
+
+
+# ------------------------------------------------------------------ patchers
+def test_patch_swaps_classes_and_ignores_missing():
+    mod = types.ModuleType("__fake_stack")
+
+    class TriangleMultiplicationOutgoing:
+        pass
+
+    mod.TriangleMultiplicationOutgoing = TriangleMultiplicationOutgoing
+    sys.modules["__fake_stack"] = mod
+    try:
+        patch._patch("__fake_stack", ["TriangleMultiplicationOutgoing", "NotPresent"],
+                     ["TriangleMultiplicationIncoming"])
+        cls = mod.TriangleMultiplicationOutgoing
+        assert issubclass(cls, FastTriangleMultiplication)
+        assert not hasattr(mod, "NotPresent") and not hasattr(mod, "TriangleMultiplicationIncoming")
+        layer = cls(16, 8, some_library_kwarg=1)
+        assert layer._impl.residual is False and layer.mode == "outgoing"
+        z = torch.randn(1, 8, 8, 16)
+        assert layer(z, mask=torch.ones(1, 8, 8), chunk_size=4).shape == z.shape
+    finally:
+        sys.modules.pop("__fake_stack", None)
+    for name in ("patch_openfold", "patch_openfold3", "patch_boltz", "patch_protenix"):
+        assert callable(getattr(ftm, name))
+
+
+# ------------------------------------------------------------------ torch path vs oracle
+@pytest.mark.parametrize("mode", ["outgoing", "incoming"])
+def test_torch_backend_matches_oracle(mode):
+    from tests.helpers import compare, make_layer, make_mask, oracle_out
+    m = make_layer(mode, residual=True, d=32)
+    gen = torch.Generator().manual_seed(4)
+    z = torch.randn(1, 16, 16, 32, generator=gen)
+    mask = make_mask("tail", 1, 16, gen)
+    with torch.no_grad():
+        out = m(z, mask=mask)
+    assert out.dtype == z.dtype
+    max_abs, mean_rel = compare(out, oracle_out(m, z, mask))
+    assert max_abs < 2e-2 and mean_rel < 3e-3
+
+
+# ------------------------------------------------------------------ C ABI
+def test_c_abi_exports_every_declared_symbol():
+    """The shared library loads (no GPU needed) and exports each function the header
+    declares; nothing is called that needs a device."""
+    import ctypes
+    import os
+    import re
+    from fast_trimul_b200 import _lib
+    header = open(os.path.join(os.path.dirname(os.path.dirname(__file__)), "include",
+                               "fast_trimul_b200.h")).read()
+    declared = set(re.findall(r"\b(ftm_[a-z_0-9]+)\s*\(", header))
+    assert len(declared) >= 13
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in sorted(declared):
+        assert hasattr(lib, name), name
+    _lib.load()
+    assert _lib.status_string(0) == "ok"
+    assert set(_lib.SIGNATURES) <= declared

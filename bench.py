@@ -296,6 +296,24 @@ def bench_sweep(args, torch, layer, dev):
     return rows
 
 
+def profile_case(args):
+    """A small fixed case for profilers: a few forwards at N=args.profile_case."""
+    import torch
+    from fast_trimul_b200.plan import TriMulPlan
+    dev = torch.device("cuda", 0)
+    n = args.profile_case
+    layer = make_layer(dev)
+    layer._impl.mode = args.mode
+    z = torch.randn(1, n, n, C, device=dev).to(torch.bfloat16)
+    mask = torch.ones(1, n, n, device=dev)
+    plan = TriMulPlan(layer._impl, 1, n, torch.bfloat16)
+    out = plan.out_like()
+    for _ in range(max(2, args.steps if args.steps < 10 else 2)):
+        plan(z, mask, out=out)
+    plan.check_error()
+    print("profile case ok", n, args.mode)
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -306,7 +324,14 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEFAULT)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunks", type=int, default=4, help="channel chunks of the b all-gather (N>1)")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="N",
+                    help="run a few plain forwards at this N (for ncu captures) and exit")
+    ap.add_argument("--mode", default="outgoing", choices=["outgoing", "incoming"])
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":

@@ -70,16 +70,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the waiting thread sleeps in hardware until the
+// phase completes or ~`ns` nanoseconds pass, instead of spinning on issue slots
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for the phase of `bar` with parity `parity` to complete. Returns false
 // (after recording `code` in *err) if it did not within FTM_WAIT_NS, or if
-// another thread of the grid has already recorded an error.
+// another thread of the grid has already recorded an error. Between checks of the
+// error word and the clock the thread sleeps in try_wait (up to 20 us per call).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*reinterpret_cast<volatile int*>(err) != 0) return false;
     if (globaltimer_ns() - t0 > FTM_WAIT_NS) {
       atomicCAS(err, 0, code);
@@ -92,7 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 // issued to land, without looking at the error word.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
     if (globaltimer_ns() - t0 > FTM_WAIT_NS) return false;
   }
   return true;
@@ -267,10 +280,60 @@ __device__ __forceinline__ uint32_t sw64_off(uint32_t row, uint32_t chunk) {
   return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
 }
 
+// 8 x 16-bit values (fp16, or bf16 when `bf16`) -> fp32
+__device__ __forceinline__ void unpack8(const uint4& r, int bf16, float (&f)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float2 v;
+    if (bf16) {
+      __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[e]);
+      v = __bfloat1622float2(h);
+    } else {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[e]);
+      v = __half22float2(h);
+    }
+    f[2 * e] = v.x;
+    f[2 * e + 1] = v.y;
+  }
+}
+
 // -------------------------------------------------------------- small math
 // logistic function with the fast exp2-based exponential and approximate divide
 // (relative error ~1e-7, far below the fp16 storage rounding that follows)
 __device__ __forceinline__ float sigmoidf_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+// Logistic function using ONE special-function (MUFU) op: e = 2^(-x log2 e) on the
+// MUFU pipe, then 1/(1+e) by Newton-Raphson on the FMA pipe. Seed: the classic
+// exponent-reflection estimate r0 = bits(0x7EF311C3 - bits(d)) (relative error
+// < 1/8 for normal d), refined by three steps r <- r + r(1 - d r) (quadratic
+// convergence: 1/8 -> 1.6e-2 -> 2.4e-4 -> ~6e-8). x is clamped to [-60, 60], where
+// the logistic is 0 or 1 to far below fp16 resolution, so d stays a normal float.
+// The epilogues are MUFU-throughput-bound (16 ops/clk/SM), so this halves their cost.
+__device__ __forceinline__ float sigmoid_nr(float x) {
+  x = fminf(fmaxf(x, -60.0f), 60.0f);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.4426950408889634f));
+  const float d = 1.0f + e;
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(d));
+#pragma unroll
+  for (int i = 0; i < 3; ++i) r = fmaf(r, fmaf(-d, r, 1.0f), r);
+  return r;
+}
+
+// tanh on the special-function unit (PTX tanh.approx.f32, one MUFU op)
+__device__ __forceinline__ float tanh_mufu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// p * sigmoid(g) with sigmoid(g) = 0.5 + 0.5 tanh(g / 2): one MUFU op and three
+// FP32 ops per element (the epilogues are bound by FP32 issue and MUFU throughput)
+__device__ __forceinline__ float gated_tanh(float p, float g) {
+  const float hp = 0.5f * p;
+  return fmaf(hp, tanh_mufu(0.5f * g), hp);
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);

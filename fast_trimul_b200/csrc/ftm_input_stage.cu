@@ -8,15 +8,15 @@
 //   warp 0      TMA: z tile (2 x 16 KB, 128B-swizzled, K-major) into a ring slot;
 //               the folded weight W' = [W_ap;W_ag;W_bp;W_bg]*diag(gamma_in) (512 x 128
 //               fp16, 128 KB) is loaded once and stays resident.
-//   warps 2-5   per row: fp32 mean/variance of z*mask (the LayerNorm statistics),
-//               bf16 -> fp16 in place when z is bf16, then mark the slot ready.
+//   warps 2-5   per row: fp32 mean/variance of z*mask, then the normalised row
+//               LN(z*mask) (without gamma/beta, which are folded into W') written
+//               back in place as fp16 -- the tensor cores' B operand.
 //   warp 1      one thread issues tcgen05.mma with the WEIGHT as the A operand and the
 //               z tile as B (M = 128 channels, N = 128 positions, K = 16) so TMEM lanes
 //               are channels and columns are positions: slot 0 = [a_p | a_g], slot 1 =
 //               [b_p | b_g], 256 columns each.
 //   warps 6-13  TMEM -> registers (lane = channel, 32 positions per load);
-//               proj = m*rstd*(acc - mean*rowsum(W')) + (W beta + b),
-//               a = proj_p * sigmoid(proj_g); each warp stages a [32 channel x 32
+//               proj = acc + (W beta + b), a = proj_p * sigmoid(proj_g); each warp stages a [32 channel x 32
 //               position] block in shared memory and TMA-stores it into the channel
 //               planes a_cm[b][c][u][v].
 // The two TMEM slots are independent, so the MMA of tile t+1's a-slot overlaps the
@@ -31,9 +31,8 @@ constexpr int kZTile = 128 * kC * 2;          // 32 KB fp16 z tile
 constexpr int kWBytes = 4 * kC * kC * 2;      // 128 KB
 constexpr int kOffW = 0;
 constexpr int kOffZ = kOffW + kWBytes;
-constexpr int kOffStats = kOffZ + kInBufs * kZTile;
 constexpr int kStageBytes = 32 * 32 * 2;       // one warp's 32 channels x 32 positions
-constexpr int kOffStage = ((kOffStats + kInBufs * 128 * 8) + 1023) & ~1023;
+constexpr int kOffStage = kOffZ + kInBufs * kZTile;
 constexpr int kOffBar = kOffStage + 8 * kStageBytes;
 constexpr int kNumBars = 1 + 3 * kInBufs + 4 + 1;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
@@ -44,7 +43,8 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                    const __grid_constant__ CUtensorMap wmap,
                    const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap bmap, const float* __restrict__ mask,
-                   const float* __restrict__ u_in, const float* __restrict__ v_in,
+                   const float* __restrict__ /*u_in: unused, rows are pre-normalised*/,
+                   const float* __restrict__ v_in,
                    __half* __restrict__ a_cm, __half* __restrict__ b_cm, PosTiling tl,
                    int incoming, int z_bf16, float eps, int* err) {
   extern __shared__ uint8_t smem_raw[];
@@ -52,7 +52,6 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                                              ~uintptr_t(1023));
   uint8_t* sW = smem + kOffW;
   uint8_t* sZ = smem + kOffZ;
-  float2* sStats = reinterpret_cast<float2*>(smem + kOffStats);
   uint8_t* sStage = smem + kOffStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_full = bars;
@@ -72,7 +71,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     for (int s = 0; s < kInBufs; ++s) {
       mbar_init(&z_full[s], 1);
       mbar_init(&a_ready[s], 128);
-      mbar_init(&buf_empty[s], 1 + 8);  // MMA commit + 8 epilogue warps (stats read)
+      mbar_init(&buf_empty[s], 1);  // MMA commit: the tile was read by the tensor cores
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&tmem_full[h], 1);
@@ -165,52 +164,11 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int s = it % kInBufs;
-      if (!mbar_wait(&z_full[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_TRANSFORM, 1)))
-        break;
       int b, u0, v0;
       tl.tile(t, b, u0, v0);
       const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
       const bool valid = (u < tl.R) && (v < tl.S);
-      uint8_t* zt = sZ + s * kZTile;
-      uint4 raw[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        raw[q] = *reinterpret_cast<const uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7));
-      // single-pass statistics shifted by the row's first value (numerically stable)
-      float shift, sum = 0.f, sq = 0.f;
-      if (z_bf16) {
-        shift = __bfloat162float(reinterpret_cast<const __nv_bfloat162*>(&raw[0])->x);
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
-          uint32_t* w = reinterpret_cast<uint32_t*>(&raw[q]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(p[e]);
-            const float d0 = f.x - shift, d1 = f.y - shift;
-            sum += d0 + d1;
-            sq += d0 * d0 + d1 * d1;
-            w[e] = pack_half2(f.x, f.y);  // exact for bf16 values inside fp16 range
-          }
-        }
-      } else {
-        shift = __half2float(reinterpret_cast<const __half2*>(&raw[0])->x);
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const __half2* p = reinterpret_cast<const __half2*>(&raw[q]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(p[e]);
-            const float d0 = f.x - shift, d1 = f.y - shift;
-            sum += d0 + d1;
-            sq += d0 * d0 + d1 * d1;
-          }
-        }
-      }
-      const float inv_c = 1.0f / kC;
-      const float dm = sum * inv_c;
-      const float mean = shift + dm;
-      const float var = fmaxf(sq * inv_c - dm * dm, 0.f);
+      // the mask load is issued before the wait so its latency hides behind the TMA
       float m = 0.f;
       if (valid) {
         if (mask) {
@@ -221,14 +179,50 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           m = 1.f;
         }
       }
-      // LayerNorm(m*z) = m*rstd*(z - mean), rstd = 1/sqrt(m^2 var + eps)
-      const float rstd = rsqrtf(m * m * var + eps);
-      const float sa = m * rstd;
-      sStats[s * 128 + row] = make_float2(sa, -sa * mean);
-      if (z_bf16) {
+      if (!mbar_wait(&z_full[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_TRANSFORM, 1)))
+        break;
+      uint8_t* zt = sZ + s * kZTile;
+      uint4 raw[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
-          *reinterpret_cast<uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7)) = raw[q];
+      for (int q = 0; q < 16; ++q)
+        raw[q] = *reinterpret_cast<const uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7));
+      // two-pass LayerNorm statistics in fp32, then the normalised row
+      // LN(m*z) = m*rstd*(z - mean) (rstd = 1/sqrt(m^2 var + eps)) written back in
+      // place as fp16: the A operand the tensor cores read (gamma/beta are folded
+      // into W' and v at pack time)
+      // (eight independent partial sums keep the FP pipes busy instead of one chain)
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float f[8];
+        unpack8(raw[q], z_bf16, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ps[e] += f[e];
+      }
+      const float mean = (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]))) *
+                         (1.0f / kC);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float f[8];
+        unpack8(raw[q], z_bf16, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ps[e] = fmaf(f[e] - mean, f[e] - mean, ps[e]);
+      }
+      const float var = (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]))) *
+                        (1.0f / kC);
+      const float sa = m * rsqrtf(m * m * var + eps);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float f[8];
+        unpack8(raw[q], z_bf16, f);
+        uint4 o;
+        o.x = pack_half2((f[0] - mean) * sa, (f[1] - mean) * sa);
+        o.y = pack_half2((f[2] - mean) * sa, (f[3] - mean) * sa);
+        o.z = pack_half2((f[4] - mean) * sa, (f[5] - mean) * sa);
+        o.w = pack_half2((f[6] - mean) * sa, (f[7] - mean) * sa);
+        *reinterpret_cast<uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7)) = o;
       }
       fence_proxy_async_smem();
       mbar_arrive(&a_ready[s]);
@@ -241,23 +235,18 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     const int phalf = ew >> 2;
     const int c = quarter * 32 + lane;                 // this thread's channel
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    float up[2], vp[2], ug[2], vg[2];
+    float vp[2], vg[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      up[h] = __ldg(u_in + h * 256 + c);
       vp[h] = __ldg(v_in + h * 256 + c);
-      ug[h] = __ldg(u_in + h * 256 + 128 + c);
       vg[h] = __ldg(v_in + h * 256 + 128 + c);
     }
     uint8_t* stage = sStage + ew * kStageBytes;
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
-      const int s = it % kInBufs;
       int b, u0, v0;
       tl.tile(t, b, u0, v0);
-      if (!mbar_wait_warp(&a_ready[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_EPILOGUE, 1))) break;
-      const float2* st = sStats + s * 128;
       for (int h = 0; h < 2; ++h) {
         if (!mbar_wait_warp(&tmem_full[h], it & 1, err, err_code(KERNEL_INPUT, ROLE_EPILOGUE, 2))) {
           ok = false;
@@ -275,12 +264,9 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float2 s0 = st[p0 + i], s1 = st[p0 + i + 1];
-            const float pv0 = fmaf(s0.x, p[i], fmaf(s0.y, up[h], vp[h]));
-            const float gv0 = fmaf(s0.x, g[i], fmaf(s0.y, ug[h], vg[h]));
-            const float pv1 = fmaf(s1.x, p[i + 1], fmaf(s1.y, up[h], vp[h]));
-            const float gv1 = fmaf(s1.x, g[i + 1], fmaf(s1.y, ug[h], vg[h]));
-            packed[i / 2] = pack_half2(pv0 * sigmoidf_fast(gv0), pv1 * sigmoidf_fast(gv1));
+            const float pv0 = p[i] + vp[h], gv0 = g[i] + vg[h];
+            const float pv1 = p[i + 1] + vp[h], gv1 = g[i + 1] + vg[h];
+            packed[i / 2] = pack_half2(gated_tanh(pv0, gv0), gated_tanh(pv1, gv1));
           }
           // stage [32 channels][32 positions] (64-byte swizzle) and TMA-store it into
           // the channel planes; the previous store must have finished reading first
@@ -302,7 +288,6 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         if (lane == 0) mbar_arrive(&tmem_empty[h]);
       }
       __syncwarp();
-      if (ok && lane == 0) mbar_arrive(&buf_empty[s]);
     }
     if (lane == 0) bulk_wait0();  // stores complete before the kernel ends
   }

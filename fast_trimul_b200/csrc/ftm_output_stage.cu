@@ -82,10 +82,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   uint8_t* sSlots = smem + kOffSlots;
   float4* sStats = reinterpret_cast<float4*>(smem + kOffStats);
   float* sMask = reinterpret_cast<float*>(smem + kOffMask);
-  float* sUg = reinterpret_cast<float*>(smem + kOffUV);
-  float* sVg = sUg + kC;
-  float* sUo = sVg + kC;
-  float* sVo = sUo + kC;
+  float4* sUV = reinterpret_cast<float4*>(smem + kOffUV);  // per channel {u_g, v_g, u_o, v_o}
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_full = bars;
   uint64_t* full = bars + 1;
@@ -113,12 +110,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < kC; i += blockDim.x) {
-    sUg[i] = u_g[i];
-    sVg[i] = v_g[i];
-    sUo[i] = u_o[i];
-    sVo[i] = v_o[i];
-  }
+  for (int i = threadIdx.x; i < kC; i += blockDim.x) sUV[i] = make_float4(u_g[i], v_g[i], u_o[i], v_o[i]);
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -198,50 +190,46 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int s = it % kOutBufs;
-      if (!mbar_wait(&full[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
-        break;
       int b, u0, v0;
       tl.tile(t, b, u0, v0);
       const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
       const bool valid = (u < tl.R) && (v < tl.S);
+      float m = 0.f;  // loaded before the wait so the latency hides behind the TMA
+      if (valid) m = mask ? __ldg(mask + (static_cast<size_t>(b) * tl.R + u) * tl.S + v) : 1.f;
+      if (!mbar_wait(&full[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
+        break;
       uint8_t* zs = sSlots + s * kSlot;
       const uint8_t* xs = zs + kZTile;
-      // z row statistics (+ bf16 -> fp16 in place)
+      // z row statistics (+ bf16 -> fp16 in place); sums shifted by the row's first
+      // value, eight independent partial sums
       uint4 raw[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q)
         raw[q] = *reinterpret_cast<const uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7));
-      float shift, sum = 0.f, sq = 0.f;
-      if (z_bf16) {
-        shift = __bfloat162float(reinterpret_cast<const __nv_bfloat162*>(&raw[0])->x);
+      float f0[8];
+      unpack8(raw[0], z_bf16, f0);
+      const float shift = f0[0];
+      float s1[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, s2[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
-          uint32_t* w = reinterpret_cast<uint32_t*>(&raw[q]);
+      for (int q = 0; q < 16; ++q) {
+        float f[8];
+        unpack8(raw[q], z_bf16, f);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(p[e]);
-            const float d0 = f.x - shift, d1 = f.y - shift;
-            sum += d0 + d1;
-            sq += d0 * d0 + d1 * d1;
-            w[e] = pack_half2(f.x, f.y);
-          }
+        for (int e = 0; e < 8; ++e) {
+          const float d = f[e] - shift;
+          s1[e] += d;
+          s2[e] = fmaf(d, d, s2[e]);
         }
-      } else {
-        shift = __half2float(reinterpret_cast<const __half2*>(&raw[0])->x);
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const __half2* p = reinterpret_cast<const __half2*>(&raw[q]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(p[e]);
-            const float d0 = f.x - shift, d1 = f.y - shift;
-            sum += d0 + d1;
-            sq += d0 * d0 + d1 * d1;
-          }
+        if (z_bf16) {
+          raw[q].x = pack_half2(f[0], f[1]);
+          raw[q].y = pack_half2(f[2], f[3]);
+          raw[q].z = pack_half2(f[4], f[5]);
+          raw[q].w = pack_half2(f[6], f[7]);
         }
       }
       const float inv_c = 1.0f / kC;
+      float sum = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
+      float sq = ((s2[0] + s2[1]) + (s2[2] + s2[3])) + ((s2[4] + s2[5]) + (s2[6] + s2[7]));
       float dm = sum * inv_c;
       const float mean_z = shift + dm;
       const float var_z = fmaxf(sq * inv_c - dm * dm, 0.f);
@@ -249,19 +237,19 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const int h = row >> 6, e = row & 63;
       const uint8_t* xcol = xs + h * kHalfTile + (e & 7) * 2;
       const float xshift = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(0, e >> 3)));
-      float xs1 = 0.f, xs2 = 0.f;
+      float a1[4] = {0.f, 0.f, 0.f, 0.f}, a2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
-      for (int c = 0; c < kC; ++c) {
-        const float xv = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c, e >> 3)));
-        const float d0 = xv - xshift;
-        xs1 += d0;
-        xs2 += d0 * d0;
+      for (int c = 0; c < kC; c += 4) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float d = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c + k, e >> 3))) - xshift;
+          a1[k] += d;
+          a2[k] = fmaf(d, d, a2[k]);
+        }
       }
-      dm = xs1 * inv_c;
+      dm = ((a1[0] + a1[1]) + (a1[2] + a1[3])) * inv_c;
       const float mean_x = xshift + dm;
-      const float var_x = fmaxf(xs2 * inv_c - dm * dm, 0.f);
-      float m = 0.f;
-      if (valid) m = mask ? __ldg(mask + (static_cast<size_t>(b) * tl.R + u) * tl.S + v) : 1.f;
+      const float var_x = fmaxf(((a2[0] + a2[1]) + (a2[2] + a2[3])) * inv_c - dm * dm, 0.f);
       const float rz = rsqrtf(m * m * var_z + eps_in);
       const float sa = m * rz;
       const float rx = rsqrtf(var_x + eps_out);
@@ -318,9 +306,9 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         float r[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int n = cb * 32 + i;
-          const float g = sigmoidf_fast(fmaf(st.x, ga[i], fmaf(st.y, sUg[n], sVg[n])));
-          const float o = fmaf(st.z, oa[i], fmaf(st.w, sUo[n], sVo[n]));
+          const float4 uv = sUV[cb * 32 + i];
+          const float g = sigmoid_nr(fmaf(st.x, ga[i], fmaf(st.y, uv.x, uv.y)));
+          const float o = fmaf(st.z, oa[i], fmaf(st.w, uv.z, uv.w));
           const float dlt = g * o;
           r[i] = (residual ? fmaf(m, zv[i], dlt) : dlt) * m;
         }

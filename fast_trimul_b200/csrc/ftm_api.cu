@@ -123,17 +123,15 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
     if (!make_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pk + L.w_in, dims, strides, box))
       return FTM_LAUNCH_FAILED;
   }
-  // channel-major outputs (S, R, C, B): stores of [32 channel x 32 position] blocks
+  // channel-major outputs (S, R, C, B): stores of [32 channel x 64 position] blocks
   CUtensorMap amap, bmap;
   {
     const uint64_t R = p->rows, S = p->cols;
     const uint64_t dims[4] = {S, R, uint64_t(kC), uint64_t(p->batch)};
     const uint64_t strides[3] = {S * 2, R * S * 2, uint64_t(kC) * R * S * 2};
-    const uint32_t box[4] = {32, 1, 32, 1};
-    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, a_cm, dims, strides, box,
-                  CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, b_cm, dims, strides, box,
-                  CU_TENSOR_MAP_SWIZZLE_64B))
+    const uint32_t box[4] = {64, 1, 32, 1};
+    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, a_cm, dims, strides, box) ||
+        !make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, b_cm, dims, strides, box))
       return FTM_LAUNCH_FAILED;
   }
   const int grid = tl.tiles < sm_count(dev) ? tl.tiles : sm_count(dev);

@@ -8,14 +8,14 @@
 //   warp 0      TMA: z tile (2 x 16 KB, 128B-swizzled, K-major) into a ring slot;
 //               the folded weight W' = [W_ap;W_ag;W_bp;W_bg]*diag(gamma_in) (512 x 128
 //               fp16, 128 KB) is loaded once and stays resident.
-//   warps 2-5   per row: fp32 mean/variance of z*mask, then the normalised row
+//   warps 2-9   per row (two threads per row): fp32 mean/variance of z*mask, then the normalised row
 //               LN(z*mask) (without gamma/beta, which are folded into W') written
 //               back in place as fp16 -- the tensor cores' B operand.
 //   warp 1      one thread issues tcgen05.mma with the WEIGHT as the A operand and the
 //               z tile as B (M = 128 channels, N = 128 positions, K = 16) so TMEM lanes
 //               are channels and columns are positions: slot 0 = [a_p | a_g], slot 1 =
 //               [b_p | b_g], 256 columns each.
-//   warps 6-13  TMEM -> registers (lane = channel, 32 positions per load);
+//   warps 10-17 TMEM -> registers (lane = channel, 32 positions per load);
 //               proj = acc + (W beta + b), a = proj_p * sigmoid(proj_g); each warp stages a [32 channel x 32
 //               position] block in shared memory and TMA-stores it into the channel
 //               planes a_cm[b][c][u][v].
@@ -28,10 +28,11 @@ namespace ftm {
 namespace {
 
 constexpr int kZTile = 128 * kC * 2;          // 32 KB fp16 z tile
+constexpr int kXformWarps = 8;
 constexpr int kWBytes = 4 * kC * kC * 2;      // 128 KB
 constexpr int kOffW = 0;
 constexpr int kOffZ = kOffW + kWBytes;
-constexpr int kStageBytes = 32 * 32 * 2;       // one warp's 32 channels x 32 positions
+constexpr int kStageBytes = 32 * 64 * 2;       // one warp's 32 channels x 64 positions
 constexpr int kOffStage = kOffZ + kInBufs * kZTile;
 constexpr int kOffBar = kOffStage + 8 * kStageBytes;
 constexpr int kNumBars = 1 + 3 * kInBufs + 4 + 1;
@@ -70,7 +71,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     mbar_init(w_full, 1);
     for (int s = 0; s < kInBufs; ++s) {
       mbar_init(&z_full[s], 1);
-      mbar_init(&a_ready[s], 128);
+      mbar_init(&a_ready[s], 32 * kXformWarps);
       mbar_init(&buf_empty[s], 1);  // MMA commit: the tile was read by the tensor cores
     }
     for (int h = 0; h < 2; ++h) {
@@ -158,9 +159,13 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       umma_commit(mma_drain);
       mbar_wait_drain(mma_drain, 0);
     }
-  } else if (warp < 6) {
-    // ------------------------------------------------- LayerNorm statistics
-    const int row = threadIdx.x - 64;  // 0..127
+  } else if (warp < 2 + kXformWarps) {
+    // ------------------------------------------------- LayerNorm of each row
+    // lanes l and l^16 of a warp share one row, each owning one 64-channel half
+    // (one 128-byte swizzled K chunk); partial sums are combined by shuffle
+    const int tw = warp - 2;
+    const int row = tw * 16 + (lane & 15);
+    const int half = lane >> 4;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int s = it % kInBufs;
@@ -181,48 +186,49 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       }
       if (!mbar_wait(&z_full[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_TRANSFORM, 1)))
         break;
-      uint8_t* zt = sZ + s * kZTile;
-      uint4 raw[16];
+      uint8_t* zt = sZ + s * kZTile + half * (kZTile / 2);
+      uint4 raw[8];
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        raw[q] = *reinterpret_cast<const uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7));
+      for (int q = 0; q < 8; ++q) raw[q] = *reinterpret_cast<const uint4*>(zt + sw128_off(row, q));
       // two-pass LayerNorm statistics in fp32, then the normalised row
       // LN(m*z) = m*rstd*(z - mean) (rstd = 1/sqrt(m^2 var + eps)) written back in
-      // place as fp16: the A operand the tensor cores read (gamma/beta are folded
-      // into W' and v at pack time)
-      // (eight independent partial sums keep the FP pipes busy instead of one chain)
+      // place as fp16: the operand the tensor cores read (gamma/beta are folded into
+      // W' and v at pack time). Eight independent partial sums per thread.
       float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
+      for (int q = 0; q < 8; ++q) {
         float f[8];
         unpack8(raw[q], z_bf16, f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) ps[e] += f[e];
       }
-      const float mean = (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]))) *
-                         (1.0f / kC);
+      float tot = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      tot += __shfl_xor_sync(0xffffffffu, tot, 16);
+      const float mean = tot * (1.0f / kC);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ps[e] = 0.f;
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
+      for (int q = 0; q < 8; ++q) {
         float f[8];
         unpack8(raw[q], z_bf16, f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) ps[e] = fmaf(f[e] - mean, f[e] - mean, ps[e]);
       }
-      const float var = (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]))) *
-                        (1.0f / kC);
+      float sq = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      sq += __shfl_xor_sync(0xffffffffu, sq, 16);
+      const float var = sq * (1.0f / kC);
       const float sa = m * rsqrtf(m * m * var + eps);
+      const float sb = -mean * sa;
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
+      for (int q = 0; q < 8; ++q) {
         float f[8];
         unpack8(raw[q], z_bf16, f);
         uint4 o;
-        o.x = pack_half2((f[0] - mean) * sa, (f[1] - mean) * sa);
-        o.y = pack_half2((f[2] - mean) * sa, (f[3] - mean) * sa);
-        o.z = pack_half2((f[4] - mean) * sa, (f[5] - mean) * sa);
-        o.w = pack_half2((f[6] - mean) * sa, (f[7] - mean) * sa);
-        *reinterpret_cast<uint4*>(zt + (q >> 3) * (kZTile / 2) + sw128_off(row, q & 7)) = o;
+        o.x = pack_half2(fmaf(f[0], sa, sb), fmaf(f[1], sa, sb));
+        o.y = pack_half2(fmaf(f[2], sa, sb), fmaf(f[3], sa, sb));
+        o.z = pack_half2(fmaf(f[4], sa, sb), fmaf(f[5], sa, sb));
+        o.w = pack_half2(fmaf(f[6], sa, sb), fmaf(f[7], sa, sb));
+        *reinterpret_cast<uint4*>(zt + sw128_off(row, q)) = o;
       }
       fence_proxy_async_smem();
       mbar_arrive(&a_ready[s]);
@@ -230,7 +236,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   } else {
     // ----------------------------------------------------------------- epilogue
     // warp -> (TMEM lane quarter = 32 channels, half of the tile's 128 positions)
-    const int ew = warp - 6;
+    const int ew = warp - 2 - kXformWarps;
     const int quarter = warp & 3;
     const int phalf = ew >> 2;
     const int c = quarter * 32 + lane;                 // this thread's channel
@@ -254,30 +260,30 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         }
         tc_fence_after();
         const CUtensorMap* omap = h == 0 ? &amap : &bmap;
+        // the previous store from this warp's staging buffer must have read it
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
 #pragma unroll 1
         for (int j = 0; j < 2; ++j) {
           const int p0 = phalf * 64 + j * 32;        // first tile row of this chunk
-          const int u = u0 + p0 / tl.vt, v = v0 + p0 % tl.vt;
           float p[32], g[32];
-          tmem_ld32(lane_base + h * 256 + p0, p);
-          tmem_ld32(lane_base + h * 256 + 128 + p0, g);
+          tmem_ld32x2(lane_base + h * 256 + p0, lane_base + h * 256 + 128 + p0, p, g);
           uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float pv0 = p[i] + vp[h], gv0 = g[i] + vg[h];
-            const float pv1 = p[i + 1] + vp[h], gv1 = g[i + 1] + vg[h];
-            packed[i / 2] = pack_half2(gated_tanh(pv0, gv0), gated_tanh(pv1, gv1));
-          }
-          // stage [32 channels][32 positions] (64-byte swizzle) and TMA-store it into
-          // the channel planes; the previous store must have finished reading first
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
+          for (int i = 0; i < 32; i += 2)
+            packed[i / 2] = pack_half2(gated_tanh(p[i] + vp[h], g[i] + vg[h]),
+                                       gated_tanh(p[i + 1] + vp[h], g[i + 1] + vg[h]));
+          // staging row = channel, 64 positions (128 B, 128-byte swizzle)
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(stage + sw64_off(lane, q)) =
+            *reinterpret_cast<uint4*>(stage + sw128_off(lane, j * 4 + q)) =
                 make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        {
+          const int p0 = phalf * 64;
+          const int u = u0 + p0 / tl.vt, v = v0 + p0 % tl.vt;
           if (lane == 0 && u < tl.R && v < tl.S) {
             tma_store_4d(omap, stage, v, u, quarter * 32, b);
             bulk_commit();

@@ -30,7 +30,7 @@ struct PackedLayout {
 };
 
 constexpr int kC = 128;            // c_z == c_h supported by the tensor-core kernels
-constexpr int kInThreads = 448;    // producer, MMA, 4 transform, 8 epilogue warps
+constexpr int kInThreads = 576;    // producer, MMA, 8 transform, 8 epilogue warps
 constexpr int kInBufs = 2;
 constexpr int kOutThreads = 448;   // producer, MMA, 4 transform, 8 epilogue warps
 constexpr int kOutBufs = 2;

@@ -307,9 +307,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float4 uv = sUV[cb * 32 + i];
-          const float g = sigmoid_nr(fmaf(st.x, ga[i], fmaf(st.y, uv.x, uv.y)));
           const float o = fmaf(st.z, oa[i], fmaf(st.w, uv.z, uv.w));
-          const float dlt = g * o;
+          const float dlt = gated_tanh(o, fmaf(st.x, ga[i], fmaf(st.y, uv.x, uv.y)));
           r[i] = (residual ? fmaf(m, zv[i], dlt) : dlt) * m;
         }
         if (OUT_DT == 0) {

@@ -34,8 +34,9 @@ MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # DRAM traffic per launch from one ncu capture of each kernel (bytes read + written),
-# scaled to N=2048 by positions processed; see profiles/ for the captures.
-NCU_TRAFFIC_N2048 = {"contraction": None, "input_stage": None, "output_stage": None}
+# measured at N=2048 directly (profiles/trimul_n2048_launches.md).
+NCU_TRAFFIC_N2048 = {"contraction": 3187747072, "input_stage": 3181398272,
+                     "output_stage": 3206178304}
 
 
 def trimul_flops(batch, n, c_z=C, c_h=C):

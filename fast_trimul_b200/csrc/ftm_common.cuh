@@ -268,6 +268,20 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t taddr0, uint32_t taddr1, fl
   }
 }
 
+// 32 TMEM lanes x 16 columns, issued without waiting (pair with tmem_wait_ld)
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor (tcgen05 format, version 1) for a
 // 128-byte-swizzled tile. K-major: rows of 128 B, 8-row groups 1024 B apart

@@ -284,41 +284,50 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const float4 st = sStats[s * 128 + row];
       const float m = sMask[s * 128 + row];
       uint8_t* zs = sSlots + s * kSlot;
-#pragma unroll 1
-      for (int cb = 2 * nhalf; cb < 2 * nhalf + 2; ++cb) {
-        float ga[32], oa[32];
-        tmem_ld32(lane_base + s * 256 + cb * 32, ga);
-        tmem_ld32(lane_base + s * 256 + 128 + cb * 32, oa);
-        float zv[32];
+      // four 16-column sub-chunks per warp; the TMEM load of sub-chunk k+1 is in
+      // flight while sub-chunk k is computed
+      uint32_t gr[2][16], orr[2][16];
+      tmem_ld16_nowait(lane_base + s * 256 + nhalf * 64, gr[0]);
+      tmem_ld16_nowait(lane_base + s * 256 + 128 + nhalf * 64, orr[0]);
+      tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = cb * 4 + q;  // 16-byte chunk of the 256-byte z row
-          const uint4 zz = *reinterpret_cast<const uint4*>(zs + (chunk >> 3) * kHalfTile +
-                                                           sw128_off(row, chunk & 7));
-          const __half2* hp = reinterpret_cast<const __half2*>(&zz);
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const float2 f = __half22float2(hp[e2]);
-            zv[q * 8 + 2 * e2] = f.x;
-            zv[q * 8 + 2 * e2 + 1] = f.y;
-          }
+      for (int k = 0; k < 4; ++k) {
+        const int cur = k & 1;
+        const int n0 = nhalf * 64 + k * 16;    // first output channel of this sub-chunk
+        if (k < 3) {
+          tmem_ld16_nowait(lane_base + s * 256 + n0 + 16, gr[cur ^ 1]);
+          tmem_ld16_nowait(lane_base + s * 256 + 128 + n0 + 16, orr[cur ^ 1]);
         }
-        float r[32];
+        float zv[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float4 uv = sUV[cb * 32 + i];
-          const float o = fmaf(st.z, oa[i], fmaf(st.w, uv.z, uv.w));
-          const float dlt = gated_tanh(o, fmaf(st.x, ga[i], fmaf(st.y, uv.x, uv.y)));
+        for (int q = 0; q < 2; ++q) {
+          const int chunk = (n0 >> 3) + q;  // 16-byte chunk of the 256-byte z row
+          float f[8];
+          unpack8(*reinterpret_cast<const uint4*>(zs + (chunk >> 3) * kHalfTile +
+                                                  sw128_off(row, chunk & 7)), 0, f);
+#pragma unroll
+          for (int e2 = 0; e2 < 8; ++e2) zv[q * 8 + e2] = f[e2];
+        }
+        float r[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 uv = sUV[n0 + i];
+          const float o = fmaf(st.z, __uint_as_float(orr[cur][i]), fmaf(st.w, uv.z, uv.w));
+          const float dlt = gated_tanh(o, fmaf(st.x, __uint_as_float(gr[cur][i]), fmaf(st.y, uv.x, uv.y)));
           r[i] = (residual ? fmaf(m, zv[i], dlt) : dlt) * m;
         }
         if (OUT_DT == 0) {
-          if (valid) store_out32<OUT_DT>(out, elem0 + cb * 32, r);
+          if (valid) {
+            float4* po = reinterpret_cast<float4*>(static_cast<float*>(out) + elem0 + n0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) po[q] = make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          }
         } else {
           // 16-bit output: overwrite the z chunks just read (same thread, same
           // addresses) so the slot holds the out tile in the z tile's layout
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = cb * 4 + q;
+          for (int q = 0; q < 2; ++q) {
+            const int chunk = (n0 >> 3) + q;
             uint4 o;
             uint32_t* w = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -328,6 +337,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
             *reinterpret_cast<uint4*>(zs + (chunk >> 3) * kHalfTile + sw128_off(row, chunk & 7)) = o;
           }
         }
+        if (k < 3) tmem_wait_ld();
       }
       tc_fence_before();
       if (OUT_DT != 0) {

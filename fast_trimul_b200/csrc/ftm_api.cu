@@ -1,5 +1,7 @@
 // C ABI of fast_trimul_b200 (declared in include/fast_trimul_b200.h): argument
 // checks, TMA tensor-map construction and the launch sequence of the three stages.
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/fast_trimul_b200.h"
@@ -143,8 +145,16 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 
+// The CTA-pair kernel (256 x 256 tiles, ftm_contraction2.cu) is the default; the
+// single-CTA kernel (128 x 256 tiles) is kept for comparison: FTM_CONTRACTION=single.
+bool use_pair_contraction() {
+  const char* v = getenv("FTM_CONTRACTION");
+  return !(v && strcmp(v, "single") == 0);
+}
+
 int stage_contract(const void* A, const void* B, void* X, int L, int m, int k, int rpb, int blocks,
                    int* err, cudaStream_t stream, int dev) {
+  const bool pair = use_pair_contraction();
   CUtensorMap amap, bmap;
   {
     const uint64_t dims[3] = {uint64_t(k), uint64_t(m), uint64_t(L)};
@@ -157,15 +167,20 @@ int stage_contract(const void* A, const void* B, void* X, int L, int m, int k, i
     const uint64_t dims[4] = {uint64_t(k), uint64_t(rpb), uint64_t(L), uint64_t(blocks)};
     const uint64_t strides[3] = {uint64_t(k) * 2, uint64_t(rpb) * k * 2,
                                  uint64_t(L) * rpb * k * 2};
-    const uint32_t box[4] = {kCtBK, kCtBN, 1, 1};
+    const uint32_t box[4] = {kCtBK, pair ? 128u : uint32_t(kCtBN), 1, 1};
     if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, B, dims, strides, box))
       return FTM_LAUNCH_FAILED;
   }
   const int n = rpb * blocks;
-  const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
-  const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
-  cudaError_t e = launch_contraction(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err,
-                                     grid, stream);
+  cudaError_t e;
+  if (pair) {
+    e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err,
+                                sm_count(dev), stream);
+  } else {
+    const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
+    const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
+    e = launch_contraction(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err, grid, stream);
+  }
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 

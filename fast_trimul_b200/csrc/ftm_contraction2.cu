@@ -1,0 +1,313 @@
+// Triangle contraction on CTA pairs (sm_100a, tcgen05.mma.cta_group::2).
+//
+// Same operation as ftm_contraction.cu, X[l][i][j] = sum_k A[l][i][k] * B[l][j][k]
+// (replacing outgoing()/incoming(), fast_trimul/_kernels.py:131-162), with a
+// 256 x 256 output tile computed by two CTAs of a cluster that share one MMA:
+//   * each CTA TMA-loads only its own halves -- A rows [128 r, 128 r + 128) and
+//     B rows [128 r, 128 r + 128) of the tile -- into a 6-stage ring (32 KB/stage);
+//     the transfers of both CTAs complete on the leader CTA's full barrier
+//     (.cta_group::2 completion). No cluster multicast is used anywhere.
+//   * the leader's MMA thread issues M=256 N=256 K=16 MMAs reading A and B from
+//     both CTAs' shared memory; each CTA's TMEM receives its 128 rows.
+//   * stage release and accumulator-ready notifications reach the peer CTA by a
+//     second tcgen05.commit aimed at the peer's barrier (shared::cluster address);
+//     the peer's epilogue warps signal the leader's accumulator-empty barrier with
+//     remote mbarrier arrives.
+// Per CTA this halves the L2->SM operand traffic per FLOP of the single-CTA
+// 128 x 256 tile (64 instead of 96 bytes per MMA clock) and doubles the stage depth.
+#include "ftm_kernels.h"
+
+namespace ftm {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;   // per-CTA halves of the 256 x 256 tile
+constexpr int kStages = 6;
+constexpr int kATile = kBM * kBK * 2;          // 16 KB
+constexpr int kBTile = kBN * kBK * 2;          // 16 KB
+constexpr int kStageBytes = kATile + kBTile;
+constexpr int kOffBar = kStages * kStageBytes;
+constexpr int kNumBars = 2 * kStages + 4 + 1;
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffTmem + 16 + 1024;
+constexpr int kThreads = 192;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `p` (a local shared-memory object) in CTA `rank`
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar_cl, void* dst,
+                                                 int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cl, void* dst,
+                                                 int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on the barrier at shared::cluster address `cl` (this CTA or the peer) once
+// all previously issued pair MMAs have completed
+__device__ __forceinline__ void umma_commit_pair(uint32_t cl) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cl)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
+                        const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
+                        int M, int N, int K, int rows_per_block, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = bars;                  // leader: operands of both CTAs landed
+  uint64_t* empty = bars + kStages;       // both: stage consumed by the pair MMA
+  uint64_t* tmem_full = bars + 2 * kStages;
+  uint64_t* tmem_empty = tmem_full + 2;   // leader: 4 local + 4 peer epilogue warps
+  uint64_t* mma_drain = tmem_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 8);
+    }
+    mbar_init(mma_drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (M + 2 * kBM - 1) / (2 * kBM);
+  const int tiles_n = (N + 2 * kBN - 1) / (2 * kBN);
+  const int per_l = tiles_m * tiles_n;
+  const int ntiles = L * per_l;
+  const int nk = (K + kBK - 1) / kBK;
+  const int cid = static_cast<int>(cluster_id_x());
+  const int ncl = static_cast<int>(num_clusters_x());
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer (both CTAs)
+      tma_prefetch_desc(&amap);
+      tma_prefetch_desc(&bmap);
+      int st = 0;
+      uint32_t ph = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < ntiles; t += ncl) {
+        const int l = t / per_l;
+        const int r = t - l * per_l;
+        const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
+        const int i0 = tm * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int j0 = tn * 2 * kBN + static_cast<int>(rank) * kBN;
+        const int blk = j0 / rows_per_block, jl = j0 - blk * rows_per_block;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[st], ph ^ 1, err, err_code(KERNEL_CONTRACT, ROLE_PRODUCER, 2))) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * kStageBytes;
+          const uint32_t fb = cluster_addr(&full[st], 0);
+          if (leader) mbar_arrive_expect_tx(&full[st], 2 * kStageBytes);
+          tma_load_3d_pair(&amap, fb, sa, kb * kBK, i0, l);
+          tma_load_4d_pair(&bmap, fb, sa + kATile, kb * kBK, jl, l, blk);
+          ++issued;
+          if (++st == kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (leader) {
+        const long first = issued > kStages ? issued - kStages : 0;
+        for (long i = first; i < issued; ++i)
+          mbar_wait_drain(&full[i % kStages], static_cast<uint32_t>((i / kStages) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      // ------------------------------------------------ pair MMA issuer (leader)
+      constexpr uint32_t idesc = idesc_f16(0, 2 * kBM, 2 * kBN, 0, 0);
+      const uint32_t base = smem_u32(smem);
+      int st = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
+        const int acc = it & 1;
+        if (!mbar_wait(&tmem_empty[acc], ((it >> 1) & 1) ^ 1, err,
+                       err_code(KERNEL_CONTRACT, ROLE_MMA, 4))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * (2 * kBN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[st], ph, err, err_code(KERNEL_CONTRACT, ROLE_MMA, 5))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + st * kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = kmajor_desc(sa + kk * 32);
+            const uint64_t bd = kmajor_desc(sa + kATile + kk * 32);
+            umma_f16_pair(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(cluster_addr(&empty[st], 0));
+          umma_commit_pair(cluster_addr(&empty[st], 1));
+          if (++st == kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(cluster_addr(&tmem_full[acc], 0));
+        umma_commit_pair(cluster_addr(&tmem_full[acc], 1));
+      }
+      umma_commit_pair(cluster_addr(mma_drain, 0));
+      mbar_wait_drain(mma_drain, 0);
+    }
+  } else {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int sub = warp & 3;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(sub * 32) << 16);
+    int it = 0;
+    for (int t = cid; t < ntiles; t += ncl, ++it) {
+      const int acc = it & 1;
+      const int l = t / per_l;
+      const int r = t - l * per_l;
+      const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
+      if (!mbar_wait_warp(&tmem_full[acc], (it >> 1) & 1, err,
+                          err_code(KERNEL_CONTRACT, ROLE_EPILOGUE, 2)))
+        break;
+      tc_fence_after();
+      const int i = tm * 2 * kBM + static_cast<int>(rank) * kBM + sub * 32 + lane;
+      __half* xrow = X + (static_cast<size_t>(l) * M + i) * N;
+      uint32_t va[2][16];
+#pragma unroll 1
+      for (int ch = 0; ch < (2 * kBN) / 16; ++ch) {
+        tmem_ld16_nowait(lane_base + acc * (2 * kBN) + ch * 16, va[0]);
+        tmem_wait_ld();
+        const int j = tn * 2 * kBN + ch * 16;
+        if (i < M) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            if (j + q * 8 < N) {
+              uint4 o;
+              o.x = pack_half2(__uint_as_float(va[0][q * 8 + 0]), __uint_as_float(va[0][q * 8 + 1]));
+              o.y = pack_half2(__uint_as_float(va[0][q * 8 + 2]), __uint_as_float(va[0][q * 8 + 3]));
+              o.z = pack_half2(__uint_as_float(va[0][q * 8 + 4]), __uint_as_float(va[0][q * 8 + 5]));
+              o.w = pack_half2(__uint_as_float(va[0][q * 8 + 6]), __uint_as_float(va[0][q * 8 + 7]));
+              *reinterpret_cast<uint4*>(xrow + j + q * 8) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&tmem_empty[acc]);
+        else remote_arrive(cluster_addr(&tmem_empty[acc], 0));
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512)
+                 : "memory");
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
+                                    int L, int M, int N, int K, int rows_per_block, int* err,
+                                    int num_sms, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(contraction_pair_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const long tiles = long(L) * ((M + 255) / 256) * ((N + 255) / 256);
+  const int clusters = static_cast<int>(tiles < num_sms / 2 ? tiles : num_sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, contraction_pair_kernel, amap, bmap, X, L, M, N, K, rows_per_block,
+                         err);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace ftm

@@ -108,9 +108,11 @@ def test_golden_fixtures_d128():
 
 
 @needs_gpu
+@pytest.mark.parametrize("kernel", ["pair", "single"])
 @pytest.mark.parametrize("L,m,n,k", [(3, 64, 64, 64), (2, 200, 136, 72), (4, 256, 512, 1024),
-                                     (1, 1024, 1024, 1024), (2, 8, 8, 8)])
-def test_contraction_vs_matmul(L, m, n, k):
+                                     (1, 1024, 1024, 1024), (2, 8, 8, 8), (3, 384, 640, 200)])
+def test_contraction_vs_matmul(L, m, n, k, kernel, monkeypatch):
+    monkeypatch.setenv("FTM_CONTRACTION", kernel)
     """ftm_contraction alone against an fp32 matmul of the same fp16 operands."""
     from fast_trimul_b200 import _lib
     lib = _lib.load()
@@ -130,8 +132,10 @@ def test_contraction_vs_matmul(L, m, n, k):
 
 
 @needs_gpu
-def test_contraction_blocked_b():
+@pytest.mark.parametrize("kernel", ["pair", "single"])
+def test_contraction_blocked_b(kernel, monkeypatch):
     """B given as row blocks (the layout an all-gather of row shards produces)."""
+    monkeypatch.setenv("FTM_CONTRACTION", kernel)
     from fast_trimul_b200 import _lib
     lib = _lib.load()
     L, m, k, rpb, blocks = 3, 256, 512, 256, 2

@@ -349,7 +349,9 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEFAULT)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--chunks", type=int, default=4, help="channel chunks of the b all-gather (N>1)")
+    ap.add_argument("--chunks", type=int, default=4, help="channel chunks of the exchange (N>1)")
+    ap.add_argument("--scheme", default=None, choices=["allgather", "alltoall", "allgather_ce", "alltoall_ce"],
+                    help="multi-GPU exchange (default: allgather_ce for 2 GPUs, alltoall_ce for more)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="N",
                     help="run a few plain forwards at this N (for ncu captures) and exit")
     ap.add_argument("--mode", default="outgoing", choices=["outgoing", "incoming"])

@@ -34,10 +34,20 @@ thread_local int g_last_launches = 0;
 
 int sm_count(int dev) {
   static int cache[64] = {0};
-  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
   int n = 0;
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 0 && dev < 64) cache[dev] = n;
+  if (dev >= 0 && dev < 64 && cache[dev]) {
+    n = cache[dev];
+  } else {
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+  }
+  // FTM_MAX_SMS caps the persistent grids (e.g. to leave SMs to a concurrent
+  // communication kernel); read per call so a process can change it between calls
+  const char* cap = getenv("FTM_MAX_SMS");
+  if (cap) {
+    const int c = atoi(cap);
+    if (c >= 2 && c < n) n = c & ~1;
+  }
   return n;
 }
 
@@ -152,11 +162,19 @@ bool use_pair_contraction() {
   return !(v && strcmp(v, "single") == 0);
 }
 
-int stage_contract(const void* A, const void* B, void* X, int L, int m, int k, int rpb, int blocks,
-                   int* err, cudaStream_t stream, int dev) {
-  const bool pair = use_pair_contraction();
+int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int a_blocks, int k,
+                   int rpb, int blocks, int* err, cudaStream_t stream, int dev) {
+  const bool pair = use_pair_contraction() || a_blocks > 1;
+  const int m = a_rpb * a_blocks;
   CUtensorMap amap, bmap;
-  {
+  if (pair) {
+    const uint64_t dims[4] = {uint64_t(k), uint64_t(a_rpb), uint64_t(L), uint64_t(a_blocks)};
+    const uint64_t strides[3] = {uint64_t(k) * 2, uint64_t(a_rpb) * k * 2,
+                                 uint64_t(L) * a_rpb * k * 2};
+    const uint32_t box[4] = {kCtBK, kCtBM, 1, 1};
+    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, A, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  } else {
     const uint64_t dims[3] = {uint64_t(k), uint64_t(m), uint64_t(L)};
     const uint64_t strides[2] = {uint64_t(k) * 2, uint64_t(m) * k * 2};
     const uint32_t box[3] = {kCtBK, kCtBM, 1};
@@ -174,7 +192,7 @@ int stage_contract(const void* A, const void* B, void* X, int L, int m, int k, i
   const int n = rpb * blocks;
   cudaError_t e;
   if (pair) {
-    e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err,
+    e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, a_rpb, err,
                                 sm_count(dev), stream);
   } else {
     const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
@@ -297,7 +315,7 @@ int ftm_trimul_fwd(const ftm_problem* p, const void* z, const float* mask, const
   if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return FTM_LAUNCH_FAILED;
   const int N = p->cols, L = p->batch * kC;
   if ((st = stage_in(p, z, mask, packed, ws + w.a, ws + w.b, err, s, dev)) != FTM_OK) return st;
-  if ((st = stage_contract(ws + w.a, ws + w.b, ws + w.x, L, N, N, N, 1, err, s, dev)) != FTM_OK)
+  if ((st = stage_contract(ws + w.a, ws + w.b, ws + w.x, L, N, 1, N, N, 1, err, s, dev)) != FTM_OK)
     return st;
   if ((st = stage_out(p, z, mask, ws + w.x, packed, out, err, s, dev)) != FTM_OK) return st;
   g_last_launches = 3;
@@ -324,16 +342,26 @@ int ftm_input_stage(const ftm_problem* p, const void* z, const float* mask, cons
 int ftm_contraction(const void* A, const void* B, void* X, int32_t L, int32_t m, int32_t k,
                     int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
                     ftm_stream_t stream) {
+  return ftm_contraction_blocked(A, B, X, L, m, 1, k, b_rows_per_block, b_blocks, err_word, stream);
+}
+
+int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
+                            int32_t a_rows_per_block, int32_t a_blocks, int32_t k,
+                            int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
+                            ftm_stream_t stream) {
   g_last_launches = 0;
   if (!A || !B || !X || !err_word) return FTM_BAD_ARGUMENT;
-  if (L < 1 || m < 1 || k < 1 || b_rows_per_block < 1 || b_blocks < 1) return FTM_BAD_SHAPE;
+  if (L < 1 || a_rows_per_block < 1 || a_blocks < 1 || k < 1 || b_rows_per_block < 1 ||
+      b_blocks < 1)
+    return FTM_BAD_SHAPE;
   if (k % 8 != 0 || (b_rows_per_block * b_blocks) % 8 != 0) return FTM_BAD_SHAPE;
   if (b_blocks > 1 && b_rows_per_block % kCtBN != 0) return FTM_BAD_SHAPE;
+  if (a_blocks > 1 && a_rows_per_block % kCtBM != 0) return FTM_BAD_SHAPE;
   if (!aligned16(A) || !aligned16(B) || !aligned16(X)) return FTM_BAD_ALIGN;
   int dev;
   if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
-  const int st = stage_contract(A, B, X, L, m, k, b_rows_per_block, b_blocks, err_word,
-                                reinterpret_cast<cudaStream_t>(stream), dev);
+  const int st = stage_contract(A, B, X, L, a_rows_per_block, a_blocks, k, b_rows_per_block,
+                                b_blocks, err_word, reinterpret_cast<cudaStream_t>(stream), dev);
   if (st == FTM_OK) g_last_launches = 1;
   return st;
 }

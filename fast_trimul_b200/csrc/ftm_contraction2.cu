@@ -7,6 +7,8 @@
 //     B rows [128 r, 128 r + 128) of the tile -- into a 6-stage ring (32 KB/stage);
 //     the transfers of both CTAs complete on the leader CTA's full barrier
 //     (.cta_group::2 completion). No cluster multicast is used anywhere.
+//     A (with X) and B may each be stored as row blocks -- the layouts that NCCL
+//     all-gathers / all-to-alls between row shards and channel shards produce.
 //   * the leader's MMA thread issues M=256 N=256 K=16 MMAs reading A and B from
 //     both CTAs' shared memory; each CTA's TMEM receives its 128 rows.
 //   * stage release and accumulator-ready notifications reach the peer CTA by a
@@ -60,14 +62,6 @@ __device__ __forceinline__ void remote_arrive(uint32_t cl_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
                : "memory");
 }
-__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar_cl, void* dst,
-                                                 int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
 __device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cl, void* dst,
                                                  int c0, int c1, int c2, int c3) {
   asm volatile(
@@ -95,7 +89,8 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cl) {
 __global__ void __launch_bounds__(kThreads, 1)
 contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
                         const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
-                        int M, int N, int K, int rows_per_block, int* err) {
+                        int M, int N, int K, int rows_per_block, int a_rows_per_block,
+                        int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -158,6 +153,7 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         const int r = t - l * per_l;
         const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
         const int i0 = tm * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int ablk = i0 / a_rows_per_block, ail = i0 - ablk * a_rows_per_block;
         const int j0 = tn * 2 * kBN + static_cast<int>(rank) * kBN;
         const int blk = j0 / rows_per_block, jl = j0 - blk * rows_per_block;
         for (int kb = 0; kb < nk; ++kb) {
@@ -168,7 +164,7 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
           uint8_t* sa = smem + st * kStageBytes;
           const uint32_t fb = cluster_addr(&full[st], 0);
           if (leader) mbar_arrive_expect_tx(&full[st], 2 * kStageBytes);
-          tma_load_3d_pair(&amap, fb, sa, kb * kBK, i0, l);
+          tma_load_4d_pair(&amap, fb, sa, kb * kBK, ail, l, ablk);
           tma_load_4d_pair(&bmap, fb, sa + kATile, kb * kBK, jl, l, blk);
           ++issued;
           if (++st == kStages) {
@@ -243,7 +239,9 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         break;
       tc_fence_after();
       const int i = tm * 2 * kBM + static_cast<int>(rank) * kBM + sub * 32 + lane;
-      __half* xrow = X + (static_cast<size_t>(l) * M + i) * N;
+      // X rows are stored in blocks of a_rows_per_block like A: [block][l][row][col]
+      const int xb = i / a_rows_per_block, xi = i - xb * a_rows_per_block;
+      __half* xrow = X + ((static_cast<size_t>(xb) * L + l) * a_rows_per_block + xi) * N;
       uint32_t va[2][16];
 #pragma unroll 1
       for (int ch = 0; ch < (2 * kBN) / 16; ++ch) {
@@ -285,7 +283,8 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
 }  // namespace
 
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
-                                    int L, int M, int N, int K, int rows_per_block, int* err,
+                                    int L, int M, int N, int K, int rows_per_block,
+                                    int a_rows_per_block, int* err,
                                     int num_sms, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(contraction_pair_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -305,7 +304,7 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, contraction_pair_kernel, amap, bmap, X, L, M, N, K, rows_per_block,
-                         err);
+                         a_rows_per_block, err);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

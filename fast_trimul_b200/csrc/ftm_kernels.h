@@ -53,7 +53,8 @@ cudaError_t launch_contraction(const CUtensorMap& amap, const CUtensorMap& bmap,
                                cudaStream_t stream);
 
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
-                                    int L, int M, int N, int K, int rows_per_block, int* err,
+                                    int L, int M, int N, int K, int rows_per_block,
+                                    int a_rows_per_block, int* err,
                                     int num_sms, cudaStream_t stream);
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,

@@ -55,10 +55,11 @@ class NativeStageOps:
                                             self.packed.data_ptr(), a.data_ptr(), b.data_ptr(),
                                             self.err.data_ptr(), self._s()), "ftm_input_stage")
 
-    def contraction(self, a, bblk, x, L, rows, n, blocks):
-        _lib.check(self.lib.ftm_contraction(a.data_ptr(), bblk.data_ptr(), x.data_ptr(), L, rows, n,
-                                            rows, blocks, self.err.data_ptr(), self._s()),
-                   "ftm_contraction")
+    def contraction(self, a, bblk, x, L, rows, n, blocks, a_blocks=1):
+        _lib.check(self.lib.ftm_contraction_blocked(a.data_ptr(), bblk.data_ptr(), x.data_ptr(), L,
+                                                    rows, a_blocks, n, rows, blocks,
+                                                    self.err.data_ptr(), self._s()),
+                   "ftm_contraction_blocked")
 
     def output_stage(self, prob, z, mask, x, out):
         _lib.check(self.lib.ftm_output_stage(prob, z.data_ptr(), None if mask is None else mask.data_ptr(),
@@ -95,10 +96,12 @@ class TorchStageOps:
         a.copy_(av.permute(0, 3, 1, 2).reshape(-1).to(a.dtype))
         b.copy_(bv.permute(0, 3, 1, 2).reshape(-1).to(b.dtype))
 
-    def contraction(self, a, bblk, x, L, rows, n, blocks):
-        A = a.view(L, rows, n).float()
-        Bf = bblk.view(blocks, L, rows, n).permute(1, 0, 2, 3).reshape(L, blocks * rows, n).float()
-        x.view(L, rows, blocks * rows).copy_(torch.bmm(A, Bf.transpose(1, 2)).to(x.dtype))
+    def contraction(self, a, bblk, x, L, rows, n, blocks, a_blocks=1):
+        def unblock(t, nb):
+            return t.view(nb, L, rows, n).permute(1, 0, 2, 3).reshape(L, nb * rows, n).float()
+        A, Bf = unblock(a, a_blocks), unblock(bblk, blocks)
+        X = torch.bmm(A, Bf.transpose(1, 2))                       # (L, a_blocks*rows, n)
+        x.view(a_blocks, L, rows, n).copy_(X.view(L, a_blocks, rows, n).permute(1, 0, 2, 3).to(x.dtype))
 
     def output_stage(self, prob, z, mask, x, out):
         import torch.nn.functional as F
@@ -117,6 +120,67 @@ class TorchStageOps:
         pass
 
 
+SCHEMES = ("allgather", "alltoall", "allgather_ce", "alltoall_ce")
+
+
+def default_scheme(world):
+    """Copy-engine exchanges; all-gather of b moves fewer bytes at 2 ranks, the
+    channel-sharded all-to-all from 4 ranks on (measured N=2048: 2 GPUs 1408 vs
+    1228 TFLOP/s, 4 GPUs 1961 vs 1662)."""
+    return "allgather_ce" if world <= 2 else "alltoall_ce"
+
+
+class PeerWindow:
+    """A device buffer on every rank, with every peer's copy mapped into this process
+    (CUDA IPC), so copy engines can write straight into a peer's buffer over NVLink."""
+
+    def __init__(self, nbytes, device, group=None):
+        from cuda.bindings import driver as drv
+        from cuda.bindings import runtime as rt
+        self.rt = rt
+        self.tensor = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        ptr = self.tensor.data_ptr()
+        err, base, _ = drv.cuMemGetAddressRange(ptr)
+        if int(err) != 0:
+            raise RuntimeError(f"cuMemGetAddressRange failed ({err})")
+        err, handle = rt.cudaIpcGetMemHandle(int(base))
+        if int(err) != 0:
+            raise RuntimeError(f"cudaIpcGetMemHandle failed ({err})")
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        infos = [None] * world
+        dist.all_gather_object(infos, (bytes(handle.reserved), ptr - int(base)), group=group)
+        self.ptrs, self._opened = [], []
+        for r, (hb, off) in enumerate(infos):
+            if r == rank:
+                self.ptrs.append(ptr)
+                continue
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = hb
+            err, p = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+            if int(err) != 0:
+                raise RuntimeError(f"cudaIpcOpenMemHandle failed ({err})")
+            self._opened.append(int(p))
+            self.ptrs.append(int(p) + off)
+
+    def close(self):
+        for p in self._opened:
+            self.rt.cudaIpcCloseMemHandle(p)
+        self._opened = []
+
+
+def PeerWindow_rt():
+    from cuda.bindings import runtime as rt
+    return rt
+
+
+def _copy_async(rt, dst, src, nbytes, stream):
+    err, = rt.cudaMemcpyAsync(dst, src, nbytes, rt.cudaMemcpyKind.cudaMemcpyDefault,
+                              rt.cudaStream_t(stream))
+    if int(err) != 0:
+        raise RuntimeError(f"cudaMemcpyAsync failed ({err})")
+
+
 class RowShardedTriMul:
     """Outgoing TriMul with z's rows sharded over the ranks of `group`.
 
@@ -126,7 +190,7 @@ class RowShardedTriMul:
     """
 
     def __init__(self, impl, batch, n, group=None, z_dtype=torch.bfloat16, out_dtype=None,
-                 chunks=4, device=None, ops=None):
+                 chunks=4, device=None, ops=None, scheme="allgather"):
         if impl.mode != "outgoing":
             raise NotImplementedError("row sharding covers outgoing mode")
         self.impl, self.group = impl, group
@@ -140,8 +204,11 @@ class RowShardedTriMul:
             # ftm_contraction reads gathered b blocks whole 256-row tiles at a time
             raise ValueError("each rank's row block must be a multiple of 256 rows")
         L = batch * C
-        if L % chunks:
-            raise ValueError("channel chunks must divide batch * 128")
+        if scheme not in SCHEMES:
+            raise ValueError(f"scheme must be one of {SCHEMES}")
+        self.scheme = scheme
+        if L % (chunks * (self.world if scheme.startswith("alltoall") else 1)):
+            raise ValueError("channel chunks (x ranks for alltoall) must divide batch * 128")
         self.L, self.chunks, self.lc = L, chunks, L // chunks
         dev = torch.device(device) if device is not None else impl.proj_a.weight.device
         self.device = dev
@@ -153,14 +220,46 @@ class RowShardedTriMul:
         plane = L * self.rows * n
         self.a = torch.empty(plane, dtype=torch.float16, device=dev)
         self.b = torch.empty(plane, dtype=torch.float16, device=dev)
-        self.x = torch.empty(plane, dtype=torch.float16, device=dev)
-        # gathered b, chunk-major: [chunk][rank][lc][rows][n]
-        self.bg = torch.empty(chunks * self.world * self.lc * self.rows * n, dtype=torch.float16,
-                              device=dev)
+        if scheme == "allgather_ce":
+            self.x = torch.empty(plane, dtype=torch.float16, device=dev)
+            # gathered b window, chunk-major [chunk][src rank][lc][rows][n], written by
+            # the peers' copy engines
+            self.win_b = PeerWindow(chunks * self.world * self.lc * self.rows * n * 2, dev, group)
+            self.bg = self.win_b.tensor.view(torch.float16)
+            self.copy_stream = torch.cuda.Stream(dev)
+            self.peer_streams = [torch.cuda.Stream(dev)]
+            self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        elif scheme == "allgather":
+            self.x = torch.empty(plane, dtype=torch.float16, device=dev)
+            # gathered b, chunk-major: [chunk][rank][lc][rows][n]
+            self.bg = torch.empty(chunks * self.world * self.lc * self.rows * n,
+                                  dtype=torch.float16, device=dev)
+        elif scheme == "alltoall_ce":
+            # receive windows written by the peers' copy engines (CUDA IPC mappings)
+            self.win_a = PeerWindow(plane * 2, dev, group)
+            self.win_b = PeerWindow(plane * 2, dev, group)
+            self.win_x = PeerWindow(plane * 2, dev, group)
+            self.ar = self.win_a.tensor.view(torch.float16)
+            self.br = self.win_b.tensor.view(torch.float16)
+            self.xr = self.win_x.tensor.view(torch.float16)
+            self.xb = torch.empty(plane, dtype=torch.float16, device=dev)
+            self.copy_stream = torch.cuda.Stream(dev)
+            self.peer_streams = [torch.cuda.Stream(dev)]   # local-block copies
+            self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        else:
+            # channel-sharded buffers (same size as a plane each): received a and b
+            # [chunk][src rank][lc / P][rows][n], x blocked by row owner, x returned
+            self.ar = torch.empty(plane, dtype=torch.float16, device=dev)
+            self.br = torch.empty(plane, dtype=torch.float16, device=dev)
+            self.xb = torch.empty(plane, dtype=torch.float16, device=dev)
+            self.xr = torch.empty(plane, dtype=torch.float16, device=dev)
 
     def comm_bytes_per_step(self):
         """Bytes each rank receives over the interconnect per forward."""
-        return (self.world - 1) * self.L * self.rows * self.n * 2
+        plane = self.L * self.rows * self.n * 2
+        if self.scheme.startswith("allgather"):
+            return (self.world - 1) * plane
+        return 3 * plane * (self.world - 1) // self.world      # a, b in and x back
 
     def __call__(self, z_local, mask_local=None, out=None, events=None):
         if out is None:
@@ -171,6 +270,27 @@ class RowShardedTriMul:
         self.ops.input_stage(self.prob, z_local, mask_local, self.a, self.b)
         if ev is not None:
             ev[1].record()
+        if self.scheme == "allgather":
+            self._exchange_allgather()
+        elif self.scheme == "allgather_ce":
+            self._exchange_allgather_ce()
+        elif self.scheme == "alltoall":
+            self._exchange_alltoall()
+        else:
+            self._exchange_alltoall_ce()
+        if ev is not None:
+            ev[2].record()
+        self.ops.output_stage(self.prob, z_local, mask_local,
+                              self.x if self.scheme.startswith("allgather") else self.xr, out)
+        if ev is not None:
+            ev[3].record()
+        if isinstance(self.ops, NativeStageOps):
+            _lib.stats["calls"] += 1
+            _lib.stats["kernel_launches"] += 2 + self.chunks
+        return out
+
+    def _exchange_allgather(self):
+        """All-gather b chunk by chunk; contract each chunk as soon as it lands."""
         blk = self.lc * self.rows * self.n
         works = []
         for k in range(self.chunks):
@@ -184,19 +304,121 @@ class RowShardedTriMul:
         for k in range(self.chunks):
             if works[k] is not None:
                 works[k].wait()
-            bsrc = self.bg[k * self.world * blk:(k + 1) * self.world * blk]
-            self.ops.contraction(self.a[k * blk:(k + 1) * blk], bsrc,
-                                 self.x[k * self.lc * self.rows * self.n:(k + 1) * self.lc * self.rows * self.n],
-                                 self.lc, self.rows, self.n, self.world)
-        if ev is not None:
-            ev[2].record()
-        self.ops.output_stage(self.prob, z_local, mask_local, self.x, out)
-        if ev is not None:
-            ev[3].record()
-        if isinstance(self.ops, NativeStageOps):
-            _lib.stats["calls"] += 1
-            _lib.stats["kernel_launches"] += 2 + self.chunks
-        return out
+            self.ops.contraction(self.a[k * blk:(k + 1) * blk],
+                                 self.bg[k * self.world * blk:(k + 1) * self.world * blk],
+                                 self.x[k * blk:(k + 1) * blk], self.lc, self.rows, self.n,
+                                 self.world)
+
+    def _exchange_alltoall(self):
+        """Row shards -> channel shards -> row shards. Chunk k moves channels
+        [k*lc, (k+1)*lc), of which rank q receives [k*lc + q*lc/P, ...): one contiguous
+        all_to_all_single per chunk for a and b, the contraction of this rank's channels
+        over all N rows, and an all_to_all_single of x back to the row owners."""
+        P, blk = self.world, self.lc * self.rows * self.n
+        lq = self.lc // P
+        ins = []
+        for k in range(self.chunks):
+            sl = slice(k * blk, (k + 1) * blk)
+            ins.append((dist.all_to_all_single(self.ar[sl], self.a[sl], group=self.group, async_op=True),
+                        dist.all_to_all_single(self.br[sl], self.b[sl], group=self.group, async_op=True)))
+        outs = []
+        for k in range(self.chunks):
+            sl = slice(k * blk, (k + 1) * blk)
+            ins[k][0].wait()
+            ins[k][1].wait()
+            # A and B: P row blocks (one per source rank) of lq channels; X blocked by row owner
+            self.ops.contraction(self.ar[sl], self.br[sl], self.xb[sl], lq, self.rows, self.n, P,
+                                 a_blocks=P)
+            outs.append(dist.all_to_all_single(self.xr[sl], self.xb[sl], group=self.group,
+                                               async_op=True))
+        for w in outs:
+            w.wait()
+
+    def _barrier_on(self, stream):
+        """Device-side barrier: a one-element NCCL all-reduce queued on `stream`
+        completes on every rank only after all ranks' earlier work on it."""
+        with torch.cuda.stream(stream):
+            dist.all_reduce(self.flag, group=self.group)
+
+    def _shifted_copies(self, src_event, copies, blk):
+        """Copy blocks to every rank after `src_event`. NVLink copies run on the copy
+        stream in shifted order -- round s goes to rank (me + s) % P -- so at any moment
+        each GPU sends to one peer and receives from one (concurrent copies to several
+        peers measured at ~half the aggregate bandwidth of this schedule). The local
+        block is copied on a side stream. copies[q] = [(dst, src), ...] for rank q."""
+        P, me, rt = self.world, self.rank, PeerWindow_rt()
+        cs, side = self.copy_stream, self.peer_streams[0]
+        cs.wait_event(src_event)
+        side.wait_event(src_event)
+        for dst, src in copies[me]:
+            _copy_async(rt, dst, src, blk, side.cuda_stream)
+        for sft in range(1, P):
+            for dst, src in copies[(me + sft) % P]:
+                _copy_async(rt, dst, src, blk, cs.cuda_stream)
+        cs.wait_stream(side)
+
+    def _exchange_allgather_ce(self):
+        """All-gather of b by the copy engines: chunk k of this rank's b goes to block
+        `me` of chunk k in every rank's window (shifted rounds), a device-side barrier
+        per chunk, and the contraction of chunk k starts as soon as its barrier passes."""
+        P, me = self.world, self.rank
+        blk = self.lc * self.rows * self.n * 2
+        comp = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(comp)
+        b0 = self.b.data_ptr()
+        done = []
+        for k in range(self.chunks):
+            self._shifted_copies(ev, [[(self.win_b.ptrs[q] + (k * P + me) * blk, b0 + k * blk)]
+                                      for q in range(P)], blk)
+            self._barrier_on(self.copy_stream)
+            e = torch.cuda.Event()
+            e.record(self.copy_stream)
+            done.append(e)
+        elems = self.lc * self.rows * self.n
+        for k in range(self.chunks):
+            comp.wait_event(done[k])
+            self.ops.contraction(self.a[k * elems:(k + 1) * elems],
+                                 self.bg[k * P * elems:(k + 1) * P * elems],
+                                 self.x[k * elems:(k + 1) * elems], self.lc, self.rows, self.n, P)
+
+    def _exchange_alltoall_ce(self):
+        """Same data movement as _exchange_alltoall, done by the copy engines: each
+        chunk's channel shards of a and b are copied straight into the owners' receive
+        windows over NVLink (no SMs used), a device-side barrier orders them before the
+        contraction, and x blocks are copied back to the row owners the same way."""
+        P, me = self.world, self.rank
+        rows, n = self.rows, self.n
+        lq = self.lc // P
+        blk = lq * rows * n * 2                     # bytes of one (rank, chunk) block
+        comp = torch.cuda.current_stream()
+        cs = self.copy_stream
+        a0, b0, xb0 = self.a.data_ptr(), self.b.data_ptr(), self.xb.data_ptr()
+        ev_ab = torch.cuda.Event()
+        ev_ab.record(comp)                          # a, b written by the input stage
+        done = []
+        for k in range(self.chunks):
+            self._shifted_copies(
+                ev_ab, [[(self.win_a.ptrs[q] + (k * P + me) * blk, a0 + (k * P + q) * blk),
+                         (self.win_b.ptrs[q] + (k * P + me) * blk, b0 + (k * P + q) * blk)]
+                        for q in range(P)], blk)
+            self._barrier_on(cs)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+            done.append(ev)
+        for k in range(self.chunks):
+            comp.wait_event(done[k])
+            elems = self.lc * rows * n
+            sl = slice(k * elems, (k + 1) * elems)
+            self.ops.contraction(self.ar[sl], self.br[sl], self.xb[sl], lq, rows, n, P, a_blocks=P)
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            # x rows of owner p (my channels) -> p's channel-major x at my channel block
+            self._shifted_copies(
+                ev, [[(self.win_x.ptrs[p] + (k * P + me) * blk, xb0 + (k * P + p) * blk)]
+                     for p in range(P)], blk)
+        self._barrier_on(cs)
+        comp.wait_stream(cs)
 
 
 # --------------------------------------------------------------------------- bench
@@ -223,7 +445,9 @@ def bench_sharded(args, torch_mod):
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     z = torch.randn(1, hi - lo, n, C, device=dev, generator=gen).to(torch.bfloat16)
     mask = torch.ones(1, hi - lo, n, device=dev)
-    sh = RowShardedTriMul(layer._impl, 1, n, chunks=getattr(args, "chunks", 4) or 4, device=dev)
+    scheme = getattr(args, "scheme", None) or default_scheme(world)
+    sh = RowShardedTriMul(layer._impl, 1, n, chunks=getattr(args, "chunks", 4) or 4, device=dev,
+                          scheme=scheme)
     out = torch.empty_like(z)
     for _ in range(args.warmup):
         sh(z, mask, out=out)
@@ -280,7 +504,7 @@ def bench_sharded(args, torch_mod):
                             "output_stage": st[2].item()},
                "clocks": clocks, "gpu_launches": (2 + sh.chunks) * K,
                "comm": {"all_gather_bytes_recv_per_rank_per_step": sh.comm_bytes_per_step(),
-                        "chunks": sh.chunks,
+                        "chunks": sh.chunks, "scheme": sh.scheme,
                         "note": "contraction stage time includes waiting for the chunked all-gather"},
                "e2e": {"value": round(_flops(n) / (e2e_ms.item() * 1e-3) / 1e12, 3),
                        "unit": "TFLOP/s", "ms_per_step": round(e2e_ms.item(), 3),

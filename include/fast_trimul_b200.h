@@ -104,6 +104,17 @@ int ftm_contraction(const void* A, const void* B, void* X, int32_t L, int32_t m,
                     int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
                     ftm_stream_t stream);
 
+/* Contraction with A (and X) given as row blocks too: A is `a_blocks` blocks of
+ * (L, a_rows_per_block, k), X is written as `a_blocks` blocks of
+ * (L, a_rows_per_block, n) -- the layouts an NCCL all-to-all between row shards and
+ * channel shards produces and consumes. m = a_blocks * a_rows_per_block. Replaces
+ * the same reference code as ftm_contraction (_kernels.py:131-162); requires
+ * a_rows_per_block % 128 == 0 when a_blocks > 1. ftm_contraction is the a_blocks = 1 case. */
+int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
+                            int32_t a_rows_per_block, int32_t a_blocks, int32_t k,
+                            int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
+                            ftm_stream_t stream);
+
 /* Output stage: LayerNorm over c_h of x (channel-major fp16), the c_h -> c_z projection,
  * sigmoid(z_n W_g + b_g) gate, residual and mask, stored in out_dtype. Replaces
  * layer_norm + KernelLinear.raw x2 + gated_residual/gate + the mask/cast glue

@@ -21,7 +21,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, n, chunks, result_path):
+def _worker(rank, world, port, n, chunks, result_path, scheme):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -35,7 +35,7 @@ def _worker(rank, world, port, n, chunks, result_path):
         lo, hi = row_range(n, world, rank)
         sh = RowShardedTriMul(m._impl, 1, n, chunks=chunks, device="cpu",
                               z_dtype=torch.float32, out_dtype=torch.float32,
-                              ops=TorchStageOps(m._impl))
+                              ops=TorchStageOps(m._impl), scheme=scheme)
         out = sh(z[:, lo:hi].contiguous(), mask[:, lo:hi].contiguous())
         parts = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(parts, out)
@@ -45,12 +45,13 @@ def _worker(rank, world, port, n, chunks, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,chunks", [(2, 4), (2, 1)])
-def test_row_sharded_matches_oracle(tmp_path, world, chunks):
+@pytest.mark.parametrize("world,chunks,scheme", [(2, 4, "allgather"), (2, 1, "allgather"),
+                                                 (2, 4, "alltoall"), (4, 2, "alltoall")])
+def test_row_sharded_matches_oracle(tmp_path, world, chunks, scheme):
     from tests.helpers import compare, make_layer, oracle_out
     n = 16
     path = str(tmp_path / "out.npy")
-    mp.start_processes(_worker, args=(world, _free_port(), n, chunks, path), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), n, chunks, path, scheme), nprocs=world,
                        join=True, start_method="spawn")
     got = torch.from_numpy(np.load(path))
     m = make_layer("outgoing", True, d=128)

@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, path):
+def _worker(rank, world, port, path, scheme):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -38,7 +38,8 @@ def _worker(rank, world, port, path):
         mask = torch.ones(1, N, N)
         mask[:, :, N - 40:] = 0
         lo, hi = row_range(N, world, rank)
-        sh = RowShardedTriMul(m._impl, 1, N, chunks=4, device=dev, out_dtype=torch.float32)
+        sh = RowShardedTriMul(m._impl, 1, N, chunks=4, device=dev, out_dtype=torch.float32,
+                              scheme=scheme)
         out = sh(z[:, lo:hi].contiguous().to(dev), mask[:, lo:hi].contiguous().to(dev))
         sh.ops.check()
         parts = [torch.empty_like(out) for _ in range(world)]
@@ -50,10 +51,11 @@ def _worker(rank, world, port, path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_row_sharding(tmp_path):
+@pytest.mark.parametrize("scheme", ["allgather", "alltoall", "allgather_ce", "alltoall_ce"])
+def test_two_gpu_row_sharding(tmp_path, scheme):
     from tests.helpers import MAX_ABS, MEAN_REL, compare, make_layer, oracle_out
     path = str(tmp_path / "o.npy")
-    mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, join=True,
+    mp.start_processes(_worker, args=(2, _free_port(), path, scheme), nprocs=2, join=True,
                        start_method="spawn")
     got = torch.from_numpy(np.load(path))
     m = make_layer("outgoing", True)

@@ -155,6 +155,28 @@ def test_contraction_blocked_b(kernel, monkeypatch):
 
 
 @needs_gpu
+def test_contraction_blocked_a_and_x():
+    """A and X as row blocks too (the channel-sharded multi-GPU layout)."""
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    L, rpb, blocks, k = 3, 256, 3, 520
+    g = torch.Generator(device="cuda").manual_seed(9)
+    Ab = torch.randn(blocks, L, rpb, k, device="cuda", generator=g).half()
+    Bb = torch.randn(blocks, L, rpb, k, device="cuda", generator=g).half()
+    X = torch.empty(blocks, L, rpb, rpb * blocks, device="cuda", dtype=torch.half)
+    err = torch.zeros(64, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.ftm_contraction_blocked(Ab.data_ptr(), Bb.data_ptr(), X.data_ptr(), L, rpb, blocks,
+                                       k, rpb, blocks, err.data_ptr(), s) == 0
+    assert lib.ftm_check_error(err.data_ptr(), None, s) == 0
+    A = Ab.permute(1, 0, 2, 3).reshape(L, blocks * rpb, k).float()
+    B = Bb.permute(1, 0, 2, 3).reshape(L, blocks * rpb, k).float()
+    ref = torch.bmm(A, B.transpose(1, 2)).view(L, blocks, rpb, -1).permute(1, 0, 2, 3)
+    rel = ((X.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 2e-3, rel
+
+
+@needs_gpu
 def test_output_canaries_and_error_word():
     """Writes stay inside `out` (guard regions untouched) and no wait timed out."""
     from fast_trimul_b200 import _lib

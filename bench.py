@@ -349,7 +349,8 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEFAULT)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--chunks", type=int, default=4, help="channel chunks of the exchange (N>1)")
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="channel chunks of the exchange (N>1; default 4 for all-gather, 2 for all-to-all)")
     ap.add_argument("--scheme", default=None, choices=["allgather", "alltoall", "allgather_ce", "alltoall_ce"],
                     help="multi-GPU exchange (default: allgather_ce for 2 GPUs, alltoall_ce for more)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="N",

@@ -446,8 +446,8 @@ def bench_sharded(args, torch_mod):
     z = torch.randn(1, hi - lo, n, C, device=dev, generator=gen).to(torch.bfloat16)
     mask = torch.ones(1, hi - lo, n, device=dev)
     scheme = getattr(args, "scheme", None) or default_scheme(world)
-    sh = RowShardedTriMul(layer._impl, 1, n, chunks=getattr(args, "chunks", 4) or 4, device=dev,
-                          scheme=scheme)
+    chunks = getattr(args, "chunks", None) or (4 if scheme.startswith("allgather") else 2)
+    sh = RowShardedTriMul(layer._impl, 1, n, chunks=chunks, device=dev, scheme=scheme)
     out = torch.empty_like(z)
     for _ in range(args.warmup):
         sh(z, mask, out=out)

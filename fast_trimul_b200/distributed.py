@@ -503,9 +503,9 @@ def bench_sharded(args, torch_mod):
                "stage_ms": {"input_stage": st[0].item(), "contraction": st[1].item(),
                             "output_stage": st[2].item()},
                "clocks": clocks, "gpu_launches": (2 + sh.chunks) * K,
-               "comm": {"all_gather_bytes_recv_per_rank_per_step": sh.comm_bytes_per_step(),
+               "comm": {"bytes_recv_per_rank_per_step": sh.comm_bytes_per_step(),
                         "chunks": sh.chunks, "scheme": sh.scheme,
-                        "note": "contraction stage time includes waiting for the chunked all-gather"},
+                        "note": "contraction stage time includes the chunked exchange it waits on"},
                "e2e": {"value": round(_flops(n) / (e2e_ms.item() * 1e-3) / 1e12, 3),
                        "unit": "TFLOP/s", "ms_per_step": round(e2e_ms.item(), 3),
                        "steps": e2e_steps,

@@ -233,7 +233,51 @@ def bench_single(args, torch):
            "gpu_launches": 3 * K}
     res["e2e"] = bench_e2e(args, torch, layer, dev, n)
     res["sweep"] = bench_sweep(args, torch, layer, dev) if not args.no_sweep else None
+    res["trunk"] = bench_trunk(args, torch, dev) if not args.no_trunk else None
     return res
+
+
+def bench_trunk(args, torch, dev, n=384, blocks=8):
+    """8 PairFormer-style blocks, N=384, c_s=384, c_z=128, bf16,
+    all-ones masks, random weights; ms per trunk forward with plain-PyTorch TriMul
+    layers vs with FastTriangleMultiplication, everything else identical."""
+    from fast_trimul_b200.pairformer import (PairFormerTrunk, copy_trimul_weights, fast_trimul,
+                                             torch_trimul, trunk_flops_trimul)
+    torch.manual_seed(0)
+    ref = PairFormerTrunk(blocks, 384, C, torch_trimul).to(dev).to(torch.bfloat16).eval()
+    fast = PairFormerTrunk(blocks, 384, C, fast_trimul).to(dev).to(torch.bfloat16).eval()
+    for m in fast.modules():
+        if hasattr(m, "_impl"):
+            m._impl.half()                      # the TriMul weights stay fp16, as in the reference
+    copy_trimul_weights(ref, fast)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    s = torch.randn(1, n, 384, device=dev, generator=gen).to(torch.bfloat16)
+    z = torch.randn(1, n, n, C, device=dev, generator=gen).to(torch.bfloat16)
+    mask = torch.ones(1, n, n, device=dev, dtype=torch.bfloat16)
+
+    def timed(model):
+        with torch.no_grad():
+            for _ in range(3):
+                model(s, z, mask)
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(10):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                out = model(s, z, mask)
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+        return statistics.median(ts), out
+
+    ms_ref, (s_ref, z_ref) = timed(ref)
+    ms_fast, (s_fast, z_fast) = timed(fast)
+    dz = ((z_fast.float() - z_ref.float()).abs().mean() / z_ref.float().abs().mean()).item()
+    return {"config": "C4 PairFormer-style trunk, 8 blocks, N=384, c_s=384, c_z=128, bf16",
+            "ms_per_fwd_torch_trimul": round(ms_ref, 3), "ms_per_fwd_fast_trimul": round(ms_fast, 3),
+            "speedup": round(ms_ref / ms_fast, 3),
+            "trimul_tflop_per_fwd": round(trunk_flops_trimul(n, C, blocks) / 1e12, 4),
+            "z_out_mean_rel_diff": round(dz, 5)}
 
 
 def bench_e2e(args, torch, layer, dev, n):
@@ -349,6 +393,7 @@ def main():
     ap.add_argument("--n", type=int, default=N_DEFAULT)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-trunk", action="store_true")
     ap.add_argument("--chunks", type=int, default=None,
                     help="channel chunks of the exchange (N>1; default 4 for all-gather, 2 for all-to-all)")
     ap.add_argument("--scheme", default=None, choices=["allgather", "alltoall", "allgather_ce", "alltoall_ce"],
@@ -415,6 +460,8 @@ def main():
     }
     if res.get("sweep"):
         line["sweep"] = res["sweep"]
+    if res.get("trunk"):
+        line["trunk"] = res["trunk"]
     if res.get("comm"):
         line["comm"] = res["comm"]
     if world == 1 and not args.no_cpu_baseline:

@@ -371,6 +371,8 @@ def profile_case(args):
     from fast_trimul_b200.plan import TriMulPlan
     dev = torch.device("cuda", 0)
     n = args.profile_case
+    if args.profile_shard:
+        return profile_shard(args, torch, dev, n, args.profile_shard)
     layer = make_layer(dev)
     layer._impl.mode = args.mode
     z = torch.randn(1, n, n, C, device=dev).to(torch.bfloat16)
@@ -381,6 +383,37 @@ def profile_case(args):
         plan(z, mask, out=out)
     plan.check_error()
     print("profile case ok", n, args.mode)
+
+
+def profile_shard(args, torch, dev, n, P):
+    """One rank's kernels of the P-way channel-sharded forward (alltoall schemes):
+    input stage on N/P rows, the contraction of 128/P channels over all N rows with A,
+    B and X in the blocked layouts, and the output stage on N/P rows."""
+    from fast_trimul_b200 import _lib
+    from fast_trimul_b200.distributed import RowShardedTriMul, TorchStageOps  # noqa: F401
+    lib = _lib.load()
+    layer = make_layer(dev)
+    R = n // P
+    z = torch.randn(1, R, n, C, device=dev).to(torch.bfloat16)
+    mask = torch.ones(1, R, n, device=dev)
+    plane = C * R * n
+    a, b, x = (torch.empty(plane, dtype=torch.float16, device=dev) for _ in range(3))
+    ar = torch.randn(plane, device=dev).half()
+    br = torch.randn(plane, device=dev).half()
+    out = torch.empty_like(z)
+    packed = layer._impl.packed_params()[0]
+    prob = layer._impl.problem(z, torch.bfloat16)
+    err = torch.zeros(64, dtype=torch.int32, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        _lib.check(lib.ftm_input_stage(prob, z.data_ptr(), mask.data_ptr(), packed.data_ptr(),
+                                       a.data_ptr(), b.data_ptr(), err.data_ptr(), s), "input")
+        _lib.check(lib.ftm_contraction_blocked(ar.data_ptr(), br.data_ptr(), x.data_ptr(), C // P,
+                                               R, P, n, R, P, err.data_ptr(), s), "contraction")
+        _lib.check(lib.ftm_output_stage(prob, z.data_ptr(), mask.data_ptr(), x.data_ptr(),
+                                        packed.data_ptr(), out.data_ptr(), err.data_ptr(), s), "output")
+    torch.cuda.synchronize()
+    print("profile shard ok", n, P)
 
 
 # --------------------------------------------------------------------------- main
@@ -401,6 +434,9 @@ def main():
     ap.add_argument("--profile-case", type=int, default=0, metavar="N",
                     help="run a few plain forwards at this N (for ncu captures) and exit")
     ap.add_argument("--mode", default="outgoing", choices=["outgoing", "incoming"])
+    ap.add_argument("--profile-shard", type=int, default=0, metavar="P",
+                    help="with --profile-case: run one rank's kernels of the P-way channel-sharded "
+                         "forward on this GPU (no communication)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)

@@ -379,6 +379,11 @@ __device__ __forceinline__ float gated_tanh(float p, float g) {
   return fmaf(hp, tanh_mufu(0.5f * g), hp);
 }
 
+// same with both arguments already halved: hp = p / 2, hg = g / 2
+__device__ __forceinline__ float gated_tanh_half(float hp, float hg) {
+  return fmaf(hp, tanh_mufu(hg), hp);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

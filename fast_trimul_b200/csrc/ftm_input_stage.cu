@@ -244,8 +244,10 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     float vp[2], vg[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      vp[h] = __ldg(v_in + h * 256 + c);
-      vg[h] = __ldg(v_in + h * 256 + 128 + c);
+      // halves of the biases: a = h_p (1 + tanh(h_g)) with h_p = (acc_p + v_p) / 2,
+      // h_g = (acc_g + v_g) / 2 -- the logistic gate in its tanh form
+      vp[h] = 0.5f * __ldg(v_in + h * 256 + c);
+      vg[h] = 0.5f * __ldg(v_in + h * 256 + 128 + c);
     }
     uint8_t* stage = sStage + ew * kStageBytes;
     int it = 0;
@@ -271,8 +273,9 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2)
-            packed[i / 2] = pack_half2(gated_tanh(p[i] + vp[h], g[i] + vg[h]),
-                                       gated_tanh(p[i + 1] + vp[h], g[i + 1] + vg[h]));
+            packed[i / 2] = pack_half2(gated_tanh_half(fmaf(0.5f, p[i], vp[h]), fmaf(0.5f, g[i], vg[h])),
+                                       gated_tanh_half(fmaf(0.5f, p[i + 1], vp[h]),
+                                                       fmaf(0.5f, g[i + 1], vg[h])));
           // staging row = channel, 64 positions (128 B, 128-byte swizzle)
 #pragma unroll
           for (int q = 0; q < 4; ++q)

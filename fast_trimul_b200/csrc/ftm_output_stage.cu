@@ -82,7 +82,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   uint8_t* sSlots = smem + kOffSlots;
   float4* sStats = reinterpret_cast<float4*>(smem + kOffStats);
   float* sMask = reinterpret_cast<float*>(smem + kOffMask);
-  float4* sUV = reinterpret_cast<float4*>(smem + kOffUV);  // per channel {u_g, v_g, u_o, v_o}
+  // per channel {u_g/2, v_g/2, u_o, v_o} (gate constants halved for the tanh form)
+  float4* sUV = reinterpret_cast<float4*>(smem + kOffUV);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_full = bars;
   uint64_t* full = bars + 1;
@@ -110,7 +111,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < kC; i += blockDim.x) sUV[i] = make_float4(u_g[i], v_g[i], u_o[i], v_o[i]);
+  for (int i = threadIdx.x; i < kC; i += blockDim.x)
+    sUV[i] = make_float4(0.5f * u_g[i], 0.5f * v_g[i], u_o[i], v_o[i]);
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -253,7 +255,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const float rz = rsqrtf(m * m * var_z + eps_in);
       const float sa = m * rz;
       const float rx = rsqrtf(var_x + eps_out);
-      sStats[s * 128 + row] = make_float4(sa, -sa * mean_z, rx, -rx * mean_x);
+      // gate pre-activation halves: g/2 = (sa/2) acc_g + (-sa mean) (u_g/2) + v_g/2
+      sStats[s * 128 + row] = make_float4(0.5f * sa, -sa * mean_z, rx, -rx * mean_x);
       sMask[s * 128 + row] = m;
       if (z_bf16) {
 #pragma unroll
@@ -283,6 +286,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const size_t elem0 = ((static_cast<size_t>(b) * tl.R + u) * tl.S + v) * kC;
       const float4 st = sStats[s * 128 + row];
       const float m = sMask[s * 128 + row];
+      const float hm = 0.5f * m, m2 = m * m;
       uint8_t* zs = sSlots + s * kSlot;
       // four 16-column sub-chunks per warp; the TMEM load of sub-chunk k+1 is in
       // flight while sub-chunk k is computed
@@ -311,10 +315,11 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         float r[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
+          // out = m^2 z (residual) + m * o * sigmoid(g), sigmoid(g) = (1 + tanh(g/2)) / 2
           const float4 uv = sUV[n0 + i];
-          const float o = fmaf(st.z, __uint_as_float(orr[cur][i]), fmaf(st.w, uv.z, uv.w));
-          const float dlt = gated_tanh(o, fmaf(st.x, __uint_as_float(gr[cur][i]), fmaf(st.y, uv.x, uv.y)));
-          r[i] = (residual ? fmaf(m, zv[i], dlt) : dlt) * m;
+          const float hmo = hm * fmaf(st.z, __uint_as_float(orr[cur][i]), fmaf(st.w, uv.z, uv.w));
+          const float t = tanh_mufu(fmaf(st.x, __uint_as_float(gr[cur][i]), fmaf(st.y, uv.x, uv.y)));
+          r[i] = fmaf(hmo, t, residual ? fmaf(m2, zv[i], hmo) : hmo);
         }
         if (OUT_DT == 0) {
           if (valid) {

@@ -404,14 +404,17 @@ def profile_shard(args, torch, dev, n, P):
     packed = layer._impl.packed_params()[0]
     prob = layer._impl.problem(z, torch.bfloat16)
     err = torch.zeros(64, dtype=torch.int32, device=dev)
+    zst = torch.empty(R * n * 2, dtype=torch.float32, device=dev)
     s = torch.cuda.current_stream().cuda_stream
     for _ in range(2):
         _lib.check(lib.ftm_input_stage(prob, z.data_ptr(), mask.data_ptr(), packed.data_ptr(),
-                                       a.data_ptr(), b.data_ptr(), err.data_ptr(), s), "input")
+                                       a.data_ptr(), b.data_ptr(), zst.data_ptr(), err.data_ptr(), s),
+                   "input")
         _lib.check(lib.ftm_contraction_blocked(ar.data_ptr(), br.data_ptr(), x.data_ptr(), C // P,
                                                R, P, n, R, P, err.data_ptr(), s), "contraction")
         _lib.check(lib.ftm_output_stage(prob, z.data_ptr(), mask.data_ptr(), x.data_ptr(),
-                                        packed.data_ptr(), out.data_ptr(), err.data_ptr(), s), "output")
+                                        zst.data_ptr(), packed.data_ptr(), out.data_ptr(),
+                                        err.data_ptr(), s), "output")
     torch.cuda.synchronize()
     print("profile shard ok", n, P)
 

@@ -39,11 +39,11 @@ SIGNATURES = {
     "ftm_pack_params": (ctypes.c_int, [ctypes.POINTER(_vp), _i32, _i32, _i32, _vp, _vp]),
     "ftm_workspace_bytes": (_sz, [_PP]),
     "ftm_trimul_fwd": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
-    "ftm_input_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_input_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftm_contraction": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "ftm_contraction_blocked": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
                                                _vp, _vp]),
-    "ftm_output_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_output_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftm_check_error": (ctypes.c_int, [_vp, _IP, _vp]),
     "ftm_workspace_error_word": (_vp, [_PP, _vp]),
     "ftm_status_string": (ctypes.c_char_p, [ctypes.c_int]),

@@ -121,7 +121,7 @@ bool make_z_map(CUtensorMap* m, const ftm_problem* p, const void* z, bool transp
 }
 
 int stage_in(const ftm_problem* p, const void* z, const float* mask, const void* packed,
-             void* a_cm, void* b_cm, int* err, cudaStream_t stream, int dev) {
+             void* a_cm, void* b_cm, float* zstats, int* err, cudaStream_t stream, int dev) {
   PosTiling tl;
   tl.init(p->batch, p->rows, p->cols);
   const bool incoming = p->mode == FTM_INCOMING;
@@ -150,8 +150,8 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
   cudaError_t e = launch_input_stage(
       zmap, wmap, amap, bmap, mask, reinterpret_cast<const float*>(pk + L.u_in),
       reinterpret_cast<const float*>(pk + L.v_in), static_cast<__half*>(a_cm),
-      static_cast<__half*>(b_cm), tl, incoming ? 1 : 0, p->z_dtype == FTM_BF16 ? 1 : 0,
-      p->eps_in, err, grid, stream);
+      static_cast<__half*>(b_cm), reinterpret_cast<float2*>(zstats), tl, incoming ? 1 : 0,
+      p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, err, grid, stream);
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 
@@ -203,7 +203,8 @@ int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int 
 }
 
 int stage_out(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
-              const void* packed, void* out, int* err, cudaStream_t stream, int dev) {
+              const float* zstats, const void* packed, void* out, int* err, cudaStream_t stream,
+              int dev) {
   PosTiling tl;
   tl.init(p->batch, p->rows, p->cols);
   CUtensorMap zmap, xmap, wmap;
@@ -236,7 +237,8 @@ int stage_out(const ftm_problem* p, const void* z, const float* mask, const void
       return FTM_LAUNCH_FAILED;
   }
   cudaError_t e = launch_output_stage(
-      zmap, xmap, wmap, omap, mask, reinterpret_cast<const float*>(pk + L.u_g),
+      zmap, xmap, wmap, omap, mask, reinterpret_cast<const float2*>(zstats),
+      reinterpret_cast<const float*>(pk + L.u_g),
       reinterpret_cast<const float*>(pk + L.v_g), reinterpret_cast<const float*>(pk + L.u_o),
       reinterpret_cast<const float*>(pk + L.v_o), out, p->out_dtype, tl, p->residual ? 1 : 0,
       p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, p->eps_out, err, grid, stream);
@@ -244,7 +246,7 @@ int stage_out(const ftm_problem* p, const void* z, const float* mask, const void
 }
 
 struct WsLayout {
-  size_t a, b, x, err, total;
+  size_t a, b, x, stats, err, total;
 };
 
 WsLayout ws_layout(const ftm_problem* p) {
@@ -254,7 +256,8 @@ WsLayout ws_layout(const ftm_problem* p) {
   w.a = 0;
   w.b = up(plane);
   w.x = w.b + up(plane);
-  w.err = w.x + up(plane);
+  w.stats = w.x + up(plane);
+  w.err = w.stats + up(size_t(p->batch) * p->rows * p->cols * 8);
   w.total = w.err + 256;
   return w;
 }
@@ -314,27 +317,28 @@ int ftm_trimul_fwd(const ftm_problem* p, const void* z, const float* mask, const
   int* err = reinterpret_cast<int*>(ws + w.err);
   if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return FTM_LAUNCH_FAILED;
   const int N = p->cols, L = p->batch * kC;
-  if ((st = stage_in(p, z, mask, packed, ws + w.a, ws + w.b, err, s, dev)) != FTM_OK) return st;
+  float* zst = reinterpret_cast<float*>(ws + w.stats);
+  if ((st = stage_in(p, z, mask, packed, ws + w.a, ws + w.b, zst, err, s, dev)) != FTM_OK) return st;
   if ((st = stage_contract(ws + w.a, ws + w.b, ws + w.x, L, N, 1, N, N, 1, err, s, dev)) != FTM_OK)
     return st;
-  if ((st = stage_out(p, z, mask, ws + w.x, packed, out, err, s, dev)) != FTM_OK) return st;
+  if ((st = stage_out(p, z, mask, ws + w.x, zst, packed, out, err, s, dev)) != FTM_OK) return st;
   g_last_launches = 3;
   return FTM_OK;
 }
 
 int ftm_input_stage(const ftm_problem* p, const void* z, const float* mask, const void* packed,
-                    void* a_cm, void* b_cm, int* err_word, ftm_stream_t stream) {
+                    void* a_cm, void* b_cm, float* zstats, int* err_word, ftm_stream_t stream) {
   g_last_launches = 0;
   int st = check_problem(p);
   if (st != FTM_OK) return st;
-  if (!z || !packed || !a_cm || !b_cm || !err_word) return FTM_BAD_ARGUMENT;
+  if (!z || !packed || !a_cm || !b_cm || !zstats || !err_word) return FTM_BAD_ARGUMENT;
   if (!aligned16(z) || !aligned16(packed) || !aligned16(a_cm) || !aligned16(b_cm) ||
       (mask && !aligned16(mask)))
     return FTM_BAD_ALIGN;
   int dev;
   if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
-  st = stage_in(p, z, mask, packed, a_cm, b_cm, err_word, reinterpret_cast<cudaStream_t>(stream),
-                dev);
+  st = stage_in(p, z, mask, packed, a_cm, b_cm, zstats, err_word,
+                reinterpret_cast<cudaStream_t>(stream), dev);
   if (st == FTM_OK) g_last_launches = 1;
   return st;
 }
@@ -367,18 +371,19 @@ int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
 }
 
 int ftm_output_stage(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
-                     const void* packed, void* out, int* err_word, ftm_stream_t stream) {
+                     const float* zstats, const void* packed, void* out, int* err_word,
+                     ftm_stream_t stream) {
   g_last_launches = 0;
   int st = check_problem(p);
   if (st != FTM_OK) return st;
-  if (!z || !x_cm || !packed || !out || !err_word) return FTM_BAD_ARGUMENT;
+  if (!z || !x_cm || !zstats || !packed || !out || !err_word) return FTM_BAD_ARGUMENT;
   if (!aligned16(z) || !aligned16(x_cm) || !aligned16(packed) || !aligned16(out) ||
       (mask && !aligned16(mask)))
     return FTM_BAD_ALIGN;
   int dev;
   if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
-  st = stage_out(p, z, mask, x_cm, packed, out, err_word, reinterpret_cast<cudaStream_t>(stream),
-                 dev);
+  st = stage_out(p, z, mask, x_cm, zstats, packed, out, err_word,
+                 reinterpret_cast<cudaStream_t>(stream), dev);
   if (st == FTM_OK) g_last_launches = 1;
   return st;
 }

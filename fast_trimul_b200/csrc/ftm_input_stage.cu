@@ -46,8 +46,9 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                    const __grid_constant__ CUtensorMap bmap, const float* __restrict__ mask,
                    const float* __restrict__ /*u_in: unused, rows are pre-normalised*/,
                    const float* __restrict__ v_in,
-                   __half* __restrict__ a_cm, __half* __restrict__ b_cm, PosTiling tl,
-                   int incoming, int z_bf16, float eps, int* err) {
+                   __half* __restrict__ a_cm, __half* __restrict__ b_cm,
+                   float2* __restrict__ zstats, PosTiling tl, int incoming, int z_bf16, float eps,
+                   int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -174,16 +175,11 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
       const bool valid = (u < tl.R) && (v < tl.S);
       // the mask load is issued before the wait so its latency hides behind the TMA
+      // position of this row in z's natural (b, r, s) order
+      const size_t zi = incoming ? (static_cast<size_t>(b) * tl.R + v) * tl.S + u
+                                 : (static_cast<size_t>(b) * tl.R + u) * tl.S + v;
       float m = 0.f;
-      if (valid) {
-        if (mask) {
-          const size_t zi = incoming ? (static_cast<size_t>(b) * tl.R + v) * tl.S + u
-                                     : (static_cast<size_t>(b) * tl.R + u) * tl.S + v;
-          m = __ldg(mask + zi);
-        } else {
-          m = 1.f;
-        }
-      }
+      if (valid) m = mask ? __ldg(mask + zi) : 1.f;
       if (!mbar_wait(&z_full[s], (it / kInBufs) & 1, err, err_code(KERNEL_INPUT, ROLE_TRANSFORM, 1)))
         break;
       uint8_t* zt = sZ + s * kZTile + half * (kZTile / 2);
@@ -219,6 +215,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const float var = sq * (1.0f / kC);
       const float sa = m * rsqrtf(m * m * var + eps);
       const float sb = -mean * sa;
+      if (valid && half == 0) zstats[zi] = make_float2(mean, sa);   // reused by the output stage
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float f[8];
@@ -316,14 +313,14 @@ size_t input_stage_smem_bytes() { return kSmemBytes; }
 cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
                                const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
                                const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
-                               const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
-                               int grid, cudaStream_t stream) {
+                               float2* zstats, const PosTiling& tl, int incoming, int z_bf16,
+                               float eps, int* err, int grid, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
   input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, amap, bmap, mask, u_in,
-                                                               v_in, a_cm, b_cm, tl, incoming,
-                                                               z_bf16, eps, err);
+                                                               v_in, a_cm, b_cm, zstats, tl,
+                                                               incoming, z_bf16, eps, err);
   return cudaGetLastError();
 }
 

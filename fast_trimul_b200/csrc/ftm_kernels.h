@@ -45,8 +45,8 @@ size_t contraction_smem_bytes();
 cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
                                const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
                                const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
-                               const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
-                               int grid, cudaStream_t stream);
+                               float2* zstats, const PosTiling& tl, int incoming, int z_bf16,
+                               float eps, int* err, int grid, cudaStream_t stream);
 
 cudaError_t launch_contraction(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X, int L,
                                int M, int N, int K, int rows_per_block, int* err, int grid,
@@ -59,7 +59,7 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
                                 const CUtensorMap& wmap, const CUtensorMap& omap,
-                                const float* mask, const float* u_g,
+                                const float* mask, const float2* zstats, const float* u_g,
                                 const float* v_g, const float* u_o, const float* v_o, void* out,
                                 int out_dtype, const PosTiling& tl, int residual, int z_bf16,
                                 float eps_in, float eps_out, int* err, int grid,

@@ -8,7 +8,7 @@
 // GPU that loads it until the process exits.
 //
 // Limit: batch * rows * cols <= FTM_STATIC_SCRATCH_MAX_POSITIONS (65,536 positions,
-// e.g. N = 256 at B = 1), i.e. 3 * 65,536 * 128 * 2 bytes + 256 = 48 MiB per GPU.
+// e.g. N = 256 at B = 1), i.e. 3 * 65,536 * 128 * 2 + 65,536 * 8 bytes (48.5 MiB) per GPU.
 // Larger problems are rejected with FTM_BAD_WORKSPACE.
 //
 // The array is shared by every call on a device and keeps the previous call's
@@ -27,7 +27,8 @@
 namespace {
 
 constexpr size_t kPlaneBytes = size_t(FTM_STATIC_SCRATCH_MAX_POSITIONS) * ftm::kC * 2;
-constexpr size_t kScratchBytes = 3 * kPlaneBytes + 256;
+constexpr size_t kStatsBytes = size_t(FTM_STATIC_SCRATCH_MAX_POSITIONS) * 8;
+constexpr size_t kScratchBytes = 3 * kPlaneBytes + kStatsBytes + 256;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
@@ -67,12 +68,13 @@ extern "C" int ftm_trimul_fwd_static_scratch(const ftm_problem* p, const void* z
   unsigned char* a = base;
   unsigned char* b = base + kPlaneBytes;
   unsigned char* x = base + 2 * kPlaneBytes;
-  int* err = reinterpret_cast<int*>(base + 3 * kPlaneBytes);
+  float* zstats = reinterpret_cast<float*>(base + 3 * kPlaneBytes);
+  int* err = reinterpret_cast<int*>(base + 3 * kPlaneBytes + kStatsBytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return FTM_LAUNCH_FAILED;
-  int st = ftm_input_stage(p, z, mask, packed, a, b, err, stream);
+  int st = ftm_input_stage(p, z, mask, packed, a, b, zstats, err, stream);
   if (st != FTM_OK) return st;
   st = ftm_contraction(a, b, x, p->batch * ftm::kC, p->rows, p->cols, p->cols, 1, err, stream);
   if (st != FTM_OK) return st;
-  return ftm_output_stage(p, z, mask, x, packed, out, err, stream);
+  return ftm_output_stage(p, z, mask, x, zstats, packed, out, err, stream);
 }

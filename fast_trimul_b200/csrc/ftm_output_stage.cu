@@ -9,8 +9,9 @@
 //   warp 0     TMA: z tile (K-major, 128B swizzle) and the x tile straight from the
 //              channel-major x (MN-major operand: 64-position atoms x 128 channels),
 //              plus the resident folded weights [W_g diag(gamma_in); W_o diag(gamma_out)].
-//   warps 2-5  per row: LayerNorm statistics of z*mask and of x (fp32), bf16 -> fp16
-//              of z in place when needed.
+//   warps 2-5  per row: LayerNorm statistics of x (fp32), bf16 -> fp16 of z in place
+//              when needed; the statistics of z*mask come from the input stage
+//              (zstats), which normalised the same rows.
 //   warp 1     tcgen05.mma: TMEM[0:128) = z W_g'^T (K-major A), TMEM[128:256) =
 //              x W_o'^T (MN-major A); two 256-column accumulators alternate tiles.
 //   warps 6-13 epilogue (two warps per TMEM lane quarter, each owning half of the
@@ -71,10 +72,12 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                     const __grid_constant__ CUtensorMap xmap,
                     const __grid_constant__ CUtensorMap wmap,
                     const __grid_constant__ CUtensorMap omap, const float* __restrict__ mask,
+                    const float2* __restrict__ zstats,
                     const float* __restrict__ u_g, const float* __restrict__ v_g,
                     const float* __restrict__ u_o, const float* __restrict__ v_o,
                     void* __restrict__ out, PosTiling tl, int residual, int z_bf16,
-                    float eps_in, float eps_out, int* err) {
+                    float /*eps_in: applied by the input stage's zstats*/, float eps_out,
+                    int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -196,45 +199,31 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       tl.tile(t, b, u0, v0);
       const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
       const bool valid = (u < tl.R) && (v < tl.S);
-      float m = 0.f;  // loaded before the wait so the latency hides behind the TMA
-      if (valid) m = mask ? __ldg(mask + (static_cast<size_t>(b) * tl.R + u) * tl.S + v) : 1.f;
+      // mask and the z LayerNorm statistics written by the input stage, loaded before
+      // the wait so their latency hides behind the TMA
+      const size_t zi = (static_cast<size_t>(b) * tl.R + u) * tl.S + v;
+      float m = 0.f;
+      float2 zst = make_float2(0.f, 0.f);
+      if (valid) {
+        m = mask ? __ldg(mask + zi) : 1.f;
+        zst = __ldg(zstats + zi);
+      }
       if (!mbar_wait(&full[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
         break;
       uint8_t* zs = sSlots + s * kSlot;
       const uint8_t* xs = zs + kZTile;
-      // z row statistics (+ bf16 -> fp16 in place); sums shifted by the row's first
-      // value, eight independent partial sums
-      uint4 raw[16];
+      if (z_bf16) {   // bf16 -> fp16 in place (exact inside fp16 range): the MMA operand
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        raw[q] = *reinterpret_cast<const uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7));
-      float f0[8];
-      unpack8(raw[0], z_bf16, f0);
-      const float shift = f0[0];
-      float s1[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, s2[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        float f[8];
-        unpack8(raw[q], z_bf16, f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float d = f[e] - shift;
-          s1[e] += d;
-          s2[e] = fmaf(d, d, s2[e]);
-        }
-        if (z_bf16) {
-          raw[q].x = pack_half2(f[0], f[1]);
-          raw[q].y = pack_half2(f[2], f[3]);
-          raw[q].z = pack_half2(f[4], f[5]);
-          raw[q].w = pack_half2(f[6], f[7]);
+        for (int q = 0; q < 16; ++q) {
+          uint4* p = reinterpret_cast<uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7));
+          float f[8];
+          unpack8(*p, 1, f);
+          *p = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
+                          pack_half2(f[6], f[7]));
         }
       }
       const float inv_c = 1.0f / kC;
-      float sum = ((s1[0] + s1[1]) + (s1[2] + s1[3])) + ((s1[4] + s1[5]) + (s1[6] + s1[7]));
-      float sq = ((s2[0] + s2[1]) + (s2[2] + s2[3])) + ((s2[4] + s2[5]) + (s2[6] + s2[7]));
-      float dm = sum * inv_c;
-      const float mean_z = shift + dm;
-      const float var_z = fmaxf(sq * inv_c - dm * dm, 0.f);
+      float dm;
       // x column statistics: element (c, row) of the MN-major x tile
       const int h = row >> 6, e = row & 63;
       const uint8_t* xcol = xs + h * kHalfTile + (e & 7) * 2;
@@ -252,17 +241,11 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       dm = ((a1[0] + a1[1]) + (a1[2] + a1[3])) * inv_c;
       const float mean_x = xshift + dm;
       const float var_x = fmaxf(((a2[0] + a2[1]) + (a2[2] + a2[3])) * inv_c - dm * dm, 0.f);
-      const float rz = rsqrtf(m * m * var_z + eps_in);
-      const float sa = m * rz;
+      const float sa = zst.y, mean_z = zst.x;   // sa = m * rstd of z*m (input stage)
       const float rx = rsqrtf(var_x + eps_out);
       // gate pre-activation halves: g/2 = (sa/2) acc_g + (-sa mean) (u_g/2) + v_g/2
       sStats[s * 128 + row] = make_float4(0.5f * sa, -sa * mean_z, rx, -rx * mean_x);
       sMask[s * 128 + row] = m;
-      if (z_bf16) {
-#pragma unroll
-        for (int q = 0; q < 16; ++q)
-          *reinterpret_cast<uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7)) = raw[q];
-      }
       fence_proxy_async_smem();
       mbar_arrive(&a_ready[s]);
     }
@@ -381,7 +364,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
 size_t output_stage_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
-                                const CUtensorMap& wmap, const CUtensorMap& omap, const float* mask, const float* u_g,
+                                const CUtensorMap& wmap, const CUtensorMap& omap, const float* mask,
+                                const float2* zstats, const float* u_g,
                                 const float* v_g, const float* u_o, const float* v_o, void* out,
                                 int out_dtype, const PosTiling& tl, int residual, int z_bf16,
                                 float eps_in, float eps_out, int* err, int grid,
@@ -390,7 +374,7 @@ cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kOutThreads, kSmemBytes, stream>>>(zmap, xmap, wmap, omap, mask, u_g, v_g, u_o, v_o, out,
+    kern<<<grid, kOutThreads, kSmemBytes, stream>>>(zmap, xmap, wmap, omap, mask, zstats, u_g, v_g, u_o, v_o, out,
                                                     tl, residual, z_bf16, eps_in, eps_out, err);
     return cudaGetLastError();
   };

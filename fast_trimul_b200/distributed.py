@@ -46,6 +46,13 @@ class NativeStageOps:
         self.lib = _lib.load()
         self.packed = impl.packed_params()[0]
         self.err = torch.zeros(64, dtype=torch.int32, device=device)
+        self.zstats = None
+
+    def _stats(self, z):
+        n = z.shape[0] * z.shape[1] * z.shape[2] * 2
+        if self.zstats is None or self.zstats.numel() < n:
+            self.zstats = torch.empty(n, dtype=torch.float32, device=z.device)
+        return self.zstats.data_ptr()
 
     def _s(self):
         return torch.cuda.current_stream().cuda_stream
@@ -53,7 +60,8 @@ class NativeStageOps:
     def input_stage(self, prob, z, mask, a, b):
         _lib.check(self.lib.ftm_input_stage(prob, z.data_ptr(), None if mask is None else mask.data_ptr(),
                                             self.packed.data_ptr(), a.data_ptr(), b.data_ptr(),
-                                            self.err.data_ptr(), self._s()), "ftm_input_stage")
+                                            self._stats(z), self.err.data_ptr(), self._s()),
+                   "ftm_input_stage")
 
     def contraction(self, a, bblk, x, L, rows, n, blocks, a_blocks=1):
         _lib.check(self.lib.ftm_contraction_blocked(a.data_ptr(), bblk.data_ptr(), x.data_ptr(), L,
@@ -63,7 +71,8 @@ class NativeStageOps:
 
     def output_stage(self, prob, z, mask, x, out):
         _lib.check(self.lib.ftm_output_stage(prob, z.data_ptr(), None if mask is None else mask.data_ptr(),
-                                             x.data_ptr(), self.packed.data_ptr(), out.data_ptr(),
+                                             x.data_ptr(), self._stats(z), self.packed.data_ptr(),
+                                             out.data_ptr(),
                                              self.err.data_ptr(), self._s()), "ftm_output_stage")
 
     def check(self):

@@ -30,6 +30,7 @@ class TriMulPlan:
         self.a = torch.empty(plane, dtype=torch.float16, device=self.device)
         self.b = torch.empty(plane, dtype=torch.float16, device=self.device)
         self.x = torch.empty(plane, dtype=torch.float16, device=self.device)
+        self.zstats = torch.empty(batch * self.rows * n * 2, dtype=torch.float32, device=self.device)
         self.err = torch.zeros(64, dtype=torch.int32, device=self.device)
         self.packed = impl.packed_params()[0]
 
@@ -58,7 +59,7 @@ class TriMulPlan:
         if ev is not None:
             ev[0].record()
         _lib.check(lib.ftm_input_stage(p, z.data_ptr(), mptr, self.packed.data_ptr(),
-                                       self.a.data_ptr(), self.b.data_ptr(),
+                                       self.a.data_ptr(), self.b.data_ptr(), self.zstats.data_ptr(),
                                        self.err.data_ptr(), s), "ftm_input_stage")
         if ev is not None:
             ev[1].record()
@@ -69,7 +70,7 @@ class TriMulPlan:
         if ev is not None:
             ev[2].record()
         _lib.check(lib.ftm_output_stage(p, z.data_ptr(), mptr, self.x.data_ptr(),
-                                        self.packed.data_ptr(), out.data_ptr(),
+                                        self.zstats.data_ptr(), self.packed.data_ptr(), out.data_ptr(),
                                         self.err.data_ptr(), s), "ftm_output_stage")
         if ev is not None:
             ev[3].record()

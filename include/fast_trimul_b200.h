@@ -89,9 +89,12 @@ int ftm_trimul_fwd(const ftm_problem* p, const void* z, const float* mask, const
  * -> sigmoid gating, written fp16 channel-major: a_cm[b][c][u][v] with (u,v) = (i,k)
  * for outgoing and (k,i) transposed for incoming, so the contraction always reads
  * K-major operands. Replaces layer_norm + _proj_gate + gate + permute copies
- * (_kernels.py:520-524, :138-139, :155-156). */
+ * (_kernels.py:520-524, :138-139, :155-156). It also writes the LayerNorm statistics of
+ * z*mask, zstats[(b*rows + r)*cols + s] = {mean, mask * rstd} (2 floats per position),
+ * which the output stage reuses for its gate projection (the reference normalises z once,
+ * _kernels.py:520, and reuses z_norm at :527). */
 int ftm_input_stage(const ftm_problem* p, const void* z, const float* mask, const void* packed,
-                    void* a_cm, void* b_cm, int* err_word, ftm_stream_t stream);
+                    void* a_cm, void* b_cm, float* zstats, int* err_word, ftm_stream_t stream);
 
 /* Contraction: for l in [0, L): X[l][i][j] = sum_k A[l][i][k] * B[l][j][k]
  * (fp16 in, fp32 accumulate, fp16 out). A is (L, m, k) row-major; B is stored as
@@ -118,16 +121,17 @@ int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
 /* Output stage: LayerNorm over c_h of x (channel-major fp16), the c_h -> c_z projection,
  * sigmoid(z_n W_g + b_g) gate, residual and mask, stored in out_dtype. Replaces
  * layer_norm + KernelLinear.raw x2 + gated_residual/gate + the mask/cast glue
- * (_kernels.py:526-530, functional.py:24-26). */
+ * (_kernels.py:526-530, functional.py:24-26). zstats: as written by ftm_input_stage. */
 int ftm_output_stage(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
-                     const void* packed, void* out, int* err_word, ftm_stream_t stream);
+                     const float* zstats, const void* packed, void* out, int* err_word,
+                     ftm_stream_t stream);
 
 /* ---- whole forward with no allocation ---------------------------------------
  * No counterpart in the reference. For callers that cannot provide a workspace --
  * hosts with a fixed device-memory budget handed out at start-up, or hosts that may
  * not call cudaMalloc while running because it can synchronise the device. Same
  * arguments and results as ftm_trimul_fwd, but a, b, x and the error word live in a
- * device array built into the library (about 48 MiB, held by each GPU that loads the
+ * device array built into the library (about 48.5 MiB, held by each GPU that loads the
  * library until exit). Problems with batch*rows*cols > FTM_STATIC_SCRATCH_MAX_POSITIONS
  * return FTM_BAD_WORKSPACE. All calls on a device share that array: calls that overlap
  * on the GPU race and must be serialised. The first call on each device looks up the

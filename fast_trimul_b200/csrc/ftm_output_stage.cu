@@ -32,10 +32,11 @@ constexpr int kWBytes = 2 * kC * kC * 2;  // 64 KB
 constexpr int kOffW = 0;
 constexpr int kOffSlots = kOffW + kWBytes;
 constexpr int kOffStats = kOffSlots + kOutBufs * kSlot;
-constexpr int kOffMask = kOffStats + kOutBufs * 128 * 16;
-constexpr int kOffUV = kOffMask + kOutBufs * 128 * 4;
+constexpr int kStatRing = 4;  // per-tile statistics outlive their ring slot's x half
+constexpr int kOffMask = kOffStats + kStatRing * 128 * 16;
+constexpr int kOffUV = kOffMask + kStatRing * 128 * 4;
 constexpr int kOffBar = kOffUV + 4 * kC * 4;
-constexpr int kNumBars = 1 + 3 * kOutBufs + 4 + 1;
+constexpr int kNumBars = 1 + 5 * kOutBufs + 4 + 1;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmem + 16 + 1024;
 
@@ -89,10 +90,12 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   float4* sUV = reinterpret_cast<float4*>(smem + kOffUV);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_full = bars;
-  uint64_t* full = bars + 1;
-  uint64_t* a_ready = full + kOutBufs;
-  uint64_t* buf_empty = a_ready + kOutBufs;
-  uint64_t* tmem_full = buf_empty + kOutBufs;
+  uint64_t* full_x = bars + 1;           // x half of a ring slot landed
+  uint64_t* full_z = full_x + kOutBufs;  // z half landed
+  uint64_t* a_ready = full_z + kOutBufs;
+  uint64_t* x_empty = a_ready + kOutBufs;  // x half read by the MMA
+  uint64_t* z_empty = x_empty + kOutBufs;  // z half done with (epilogue stored out)
+  uint64_t* tmem_full = z_empty + kOutBufs;
   uint64_t* tmem_empty = tmem_full + 2;
   uint64_t* mma_drain = tmem_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
@@ -103,9 +106,11 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   if (threadIdx.x == 0) {
     mbar_init(w_full, 1);
     for (int s = 0; s < kOutBufs; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full_x[s], 1);
+      mbar_init(&full_z[s], 1);
       mbar_init(&a_ready[s], 128);
-      mbar_init(&buf_empty[s], 8);  // epilogue warps (they finish after the MMA read)
+      mbar_init(&x_empty[s], 1);    // MMA commit
+      mbar_init(&z_empty[s], 8);    // epilogue warps
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
@@ -124,8 +129,9 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   const int ntiles = tl.tiles;
 
   if (warp == 0) {
+    // two producer lanes: lane 0 refills x halves as soon as the MMA has read them,
+    // lane 1 refills z halves once the epilogue has stored the tile written over them
     if (lane == 0) {
-      tma_prefetch_desc(&zmap);
       tma_prefetch_desc(&xmap);
       tma_prefetch_desc(&wmap);
       mbar_arrive_expect_tx(w_full, kWBytes);
@@ -133,25 +139,39 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       int it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int s = it % kOutBufs;
-        if (!mbar_wait(&buf_empty[s], ((it / kOutBufs) & 1) ^ 1, err,
+        if (!mbar_wait(&x_empty[s], ((it / kOutBufs) & 1) ^ 1, err,
                        err_code(KERNEL_OUTPUT, ROLE_PRODUCER, 1)))
           break;
         int b, u0, v0;
         tl.tile(t, b, u0, v0);
-        uint8_t* zs = sSlots + s * kSlot;
-        uint8_t* xs = zs + kZTile;
-        mbar_arrive_expect_tx(&full[s], kSlot);
-        tma_load_4d(&zmap, &full[s], zs, 0, v0, u0, b);
-        tma_load_4d(&zmap, &full[s], zs + kHalfTile, 64, v0, u0, b);
+        uint8_t* xs = sSlots + s * kSlot + kZTile;
+        mbar_arrive_expect_tx(&full_x[s], kXTile);
         for (int h = 0; h < 2; ++h) {
           const int jj = tl.vt == 128 ? v0 + 64 * h : v0;
           const int ii = tl.vt == 128 ? u0 : u0 + h;
-          tma_load_4d(&xmap, &full[s], xs + h * kHalfTile, jj, ii, 0, b);
+          tma_load_4d(&xmap, &full_x[s], xs + h * kHalfTile, jj, ii, 0, b);
         }
       }
       for (int i = (it > kOutBufs ? it - kOutBufs : 0); i < it; ++i)
-        mbar_wait_drain(&full[i % kOutBufs], (i / kOutBufs) & 1);
+        mbar_wait_drain(&full_x[i % kOutBufs], (i / kOutBufs) & 1);
       mbar_wait_drain(w_full, 0);
+    } else if (lane == 1) {
+      tma_prefetch_desc(&zmap);
+      int it = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int s = it % kOutBufs;
+        if (!mbar_wait(&z_empty[s], ((it / kOutBufs) & 1) ^ 1, err,
+                       err_code(KERNEL_OUTPUT, ROLE_PRODUCER, 2)))
+          break;
+        int b, u0, v0;
+        tl.tile(t, b, u0, v0);
+        uint8_t* zs = sSlots + s * kSlot;
+        mbar_arrive_expect_tx(&full_z[s], kZTile);
+        tma_load_4d(&zmap, &full_z[s], zs, 0, v0, u0, b);
+        tma_load_4d(&zmap, &full_z[s], zs + kHalfTile, 64, v0, u0, b);
+      }
+      for (int i = (it > kOutBufs ? it - kOutBufs : 0); i < it; ++i)
+        mbar_wait_drain(&full_z[i % kOutBufs], (i / kOutBufs) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -186,6 +206,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           umma_f16(d + 128, ad, bd, idesc_x, kk > 0 ? 1u : 0u);
         }
         umma_commit(&tmem_full[s]);
+        umma_commit(&x_empty[s]);
       }
       umma_commit(mma_drain);
       mbar_wait_drain(mma_drain, 0);
@@ -208,20 +229,10 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         m = mask ? __ldg(mask + zi) : 1.f;
         zst = __ldg(zstats + zi);
       }
-      if (!mbar_wait(&full[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
+      if (!mbar_wait(&full_x[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
         break;
       uint8_t* zs = sSlots + s * kSlot;
       const uint8_t* xs = zs + kZTile;
-      if (z_bf16) {   // bf16 -> fp16 in place (exact inside fp16 range): the MMA operand
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          uint4* p = reinterpret_cast<uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7));
-          float f[8];
-          unpack8(*p, 1, f);
-          *p = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
-                          pack_half2(f[6], f[7]));
-        }
-      }
       const float inv_c = 1.0f / kC;
       float dm;
       // x column statistics: element (c, row) of the MN-major x tile
@@ -241,11 +252,23 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       dm = ((a1[0] + a1[1]) + (a1[2] + a1[3])) * inv_c;
       const float mean_x = xshift + dm;
       const float var_x = fmaxf(((a2[0] + a2[1]) + (a2[2] + a2[3])) * inv_c - dm * dm, 0.f);
+      if (!mbar_wait(&full_z[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 2)))
+        break;
+      if (z_bf16) {   // bf16 -> fp16 in place (exact inside fp16 range): the MMA operand
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          uint4* p = reinterpret_cast<uint4*>(zs + (q >> 3) * kHalfTile + sw128_off(row, q & 7));
+          float f[8];
+          unpack8(*p, 1, f);
+          *p = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
+                          pack_half2(f[6], f[7]));
+        }
+      }
       const float sa = zst.y, mean_z = zst.x;   // sa = m * rstd of z*m (input stage)
       const float rx = rsqrtf(var_x + eps_out);
       // gate pre-activation halves: g/2 = (sa/2) acc_g + (-sa mean) (u_g/2) + v_g/2
-      sStats[s * 128 + row] = make_float4(0.5f * sa, -sa * mean_z, rx, -rx * mean_x);
-      sMask[s * 128 + row] = m;
+      sStats[(it % kStatRing) * 128 + row] = make_float4(0.5f * sa, -sa * mean_z, rx, -rx * mean_x);
+      sMask[(it % kStatRing) * 128 + row] = m;
       fence_proxy_async_smem();
       mbar_arrive(&a_ready[s]);
     }
@@ -267,8 +290,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const int u = u0 + row / tl.vt, v = v0 + row % tl.vt;
       const bool valid = (u < tl.R) && (v < tl.S);
       const size_t elem0 = ((static_cast<size_t>(b) * tl.R + u) * tl.S + v) * kC;
-      const float4 st = sStats[s * 128 + row];
-      const float m = sMask[s * 128 + row];
+      const float4 st = sStats[(it % kStatRing) * 128 + row];
+      const float m = sMask[(it % kStatRing) * 128 + row];
       const float hm = 0.5f * m, m2 = m * m;
       uint8_t* zs = sSlots + s * kSlot;
       // four 16-column sub-chunks per warp; the TMEM load of sub-chunk k+1 is in
@@ -345,7 +368,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&tmem_empty[s]);
-        mbar_arrive(&buf_empty[s]);
+        mbar_arrive(&z_empty[s]);
       }
     }
   }

@@ -120,6 +120,13 @@ bool make_z_map(CUtensorMap* m, const ftm_problem* p, const void* z, bool transp
   return make_map(m, tma_dtype(p->z_dtype), 4, z, dims, strides, box);
 }
 
+// FTM_TEST_STALL=input makes the input stage withhold one tile load so its bounded
+// waits expire: the failure-detection test of the device error path (no fault, no trap)
+int test_stall_requested() {
+  const char* v = getenv("FTM_TEST_STALL");
+  return (v && strcmp(v, "input") == 0) ? 1 : 0;
+}
+
 int stage_in(const ftm_problem* p, const void* z, const float* mask, const void* packed,
              void* a_cm, void* b_cm, float* zstats, int* err, cudaStream_t stream, int dev) {
   PosTiling tl;
@@ -151,7 +158,7 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
       zmap, wmap, amap, bmap, mask, reinterpret_cast<const float*>(pk + L.u_in),
       reinterpret_cast<const float*>(pk + L.v_in), static_cast<__half*>(a_cm),
       static_cast<__half*>(b_cm), reinterpret_cast<float2*>(zstats), tl, incoming ? 1 : 0,
-      p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, err, grid, stream);
+      p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, err, grid, stream, test_stall_requested());
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 

@@ -271,6 +271,13 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
     }
   }
 
+  // After a failure the two CTAs may have issued different numbers of loads, and the
+  // leader's drain only covers its own: give any copy still landing in this CTA's
+  // shared memory time to finish (bounded, error path only) before leaving.
+  if (grid_failed(err)) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+  }
   tc_fence_before();
   cluster_sync_all();  // no CTA leaves while its peer may still touch its memory
   if (warp == 1) {

@@ -48,7 +48,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                    const float* __restrict__ v_in,
                    __half* __restrict__ a_cm, __half* __restrict__ b_cm,
                    float2* __restrict__ zstats, PosTiling tl, int incoming, int z_bf16, float eps,
-                   int* err) {
+                   int* err, int test_stall) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -104,6 +104,9 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         const int s = it % kInBufs;
         const uint32_t ph = (it / kInBufs) & 1;
         if (!mbar_wait(&buf_empty[s], ph ^ 1, err, err_code(KERNEL_INPUT, ROLE_PRODUCER, 1))) break;
+        // failure-detection test: CTA 0 never loads its first tile, so the waits on it
+        // must expire, record the error and let every role drain and exit
+        if (test_stall && blockIdx.x == 0) break;
         int b, u0, v0;
         tl.tile(t, b, u0, v0);
         uint8_t* dst = sZ + s * kZTile;
@@ -314,13 +317,14 @@ cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
                                const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
                                const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
                                float2* zstats, const PosTiling& tl, int incoming, int z_bf16,
-                               float eps, int* err, int grid, cudaStream_t stream) {
+                               float eps, int* err, int grid, cudaStream_t stream, int test_stall) {
   cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
   input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, amap, bmap, mask, u_in,
                                                                v_in, a_cm, b_cm, zstats, tl,
-                                                               incoming, z_bf16, eps, err);
+                                                               incoming, z_bf16, eps, err,
+                                                               test_stall);
   return cudaGetLastError();
 }
 

@@ -46,7 +46,8 @@ cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
                                const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
                                const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
                                float2* zstats, const PosTiling& tl, int incoming, int z_bf16,
-                               float eps, int* err, int grid, cudaStream_t stream);
+                               float eps, int* err, int grid, cudaStream_t stream,
+                               int test_stall = 0);
 
 cudaError_t launch_contraction(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X, int L,
                                int M, int N, int K, int rows_per_block, int* err, int grid,

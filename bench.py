@@ -365,6 +365,56 @@ def bench_sweep(args, torch, layer, dev):
     return rows
 
 
+def reference_gpu_sweep(ns):
+    """The reference's own FastTriangleMultiplication (its CuTe-DSL Ampere kernels, fp16)
+    on this GPU, imported from baseline/_ref (the reference's pure-Python package;
+    `cutlass.testing` -- imported only by its GEMM CLI harness -- is stubbed). Same
+    workload as the main line: outgoing, B=1, c=128, bf16 z, ones mask; median of 10
+    CUDA-event timed calls after warm-up, eager and after its own `graphed()` capture."""
+    import types
+    import torch
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "fast_trimul")):
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "baseline/_ref/fast_trimul missing"}))
+        return
+    sys.path.insert(0, ref_root)
+    import cutlass
+    if "cutlass.testing" not in sys.modules:
+        stub = types.ModuleType("cutlass.testing")
+        sys.modules["cutlass.testing"] = stub
+        cutlass.testing = stub
+    import fast_trimul as ref
+    from fast_trimul import FastTriangleMultiplication as RefTriMul
+    assert os.path.abspath(ref.__file__).startswith(ref_root)
+    for n in ns:
+        torch.manual_seed(0)
+        m = RefTriMul(C, C, "outgoing").cuda().eval()
+        z = torch.randn(1, n, n, C, device="cuda").to(torch.bfloat16)
+        mask = torch.ones(1, n, n, device="cuda")
+
+        def timed():
+            ts = []
+            for _ in range(10):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                m(z, mask=mask)
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+            return statistics.median(ts)
+
+        with torch.no_grad():
+            for _ in range(3):
+                m(z, mask=mask)
+            torch.cuda.synchronize()
+            eager = timed()
+            m.graphed(z, mask)
+            graphed = timed()
+        print(json.dumps({"impl": "reference-gpu", "n": n, "eager_ms": round(eager, 3),
+                          "graphed_ms": round(graphed, 3),
+                          "graphed_tflops": round(trimul_flops(1, n) / graphed / 1e9, 2)}), flush=True)
+
+
 def profile_case(args):
     """A small fixed case for profilers: a few forwards at N=args.profile_case."""
     import torch
@@ -437,12 +487,18 @@ def main():
     ap.add_argument("--profile-case", type=int, default=0, metavar="N",
                     help="run a few plain forwards at this N (for ncu captures) and exit")
     ap.add_argument("--mode", default="outgoing", choices=["outgoing", "incoming"])
+    ap.add_argument("--reference-gpu-sweep", type=int, nargs="*", default=None, metavar="N",
+                    help="time the reference's own GPU kernels (baseline/_ref, CUDA-graphed) at "
+                         "these N and print one JSON line each")
     ap.add_argument("--profile-shard", type=int, default=0, metavar="P",
                     help="with --profile-case: run one rank's kernels of the P-way channel-sharded "
                          "forward on this GPU (no communication)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
+        return
+    if args.reference_gpu_sweep is not None:
+        reference_gpu_sweep(args.reference_gpu_sweep or [256, 512, 1024, 2048])
         return
     args.warmup = max(args.warmup, 3)
 

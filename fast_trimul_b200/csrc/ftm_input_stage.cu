@@ -193,26 +193,24 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       // LN(m*z) = m*rstd*(z - mean) (rstd = 1/sqrt(m^2 var + eps)) written back in
       // place as fp16: the operand the tensor cores read (gamma/beta are folded into
       // W' and v at pack time). Eight independent partial sums per thread.
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float f[64];                         // this thread's 64 values, unpacked once
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float f[8];
-        unpack8(raw[q], z_bf16, f);
+        float t8[8];
+        unpack8(raw[q], z_bf16, t8);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ps[e] += f[e];
+        for (int e = 0; e < 8; ++e) f[q * 8 + e] = t8[e];
       }
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 64; ++i) ps[i & 7] += f[i];
       float tot = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       tot += __shfl_xor_sync(0xffffffffu, tot, 16);
       const float mean = tot * (1.0f / kC);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ps[e] = 0.f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float f[8];
-        unpack8(raw[q], z_bf16, f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ps[e] = fmaf(f[e] - mean, f[e] - mean, ps[e]);
-      }
+      for (int i = 0; i < 64; ++i) ps[i & 7] = fmaf(f[i] - mean, f[i] - mean, ps[i & 7]);
       float sq = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       sq += __shfl_xor_sync(0xffffffffu, sq, 16);
       const float var = sq * (1.0f / kC);
@@ -221,13 +219,11 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       if (valid && half == 0) zstats[zi] = make_float2(mean, sa);   // reused by the output stage
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float f[8];
-        unpack8(raw[q], z_bf16, f);
         uint4 o;
-        o.x = pack_half2(fmaf(f[0], sa, sb), fmaf(f[1], sa, sb));
-        o.y = pack_half2(fmaf(f[2], sa, sb), fmaf(f[3], sa, sb));
-        o.z = pack_half2(fmaf(f[4], sa, sb), fmaf(f[5], sa, sb));
-        o.w = pack_half2(fmaf(f[6], sa, sb), fmaf(f[7], sa, sb));
+        o.x = pack_half2(fmaf(f[q * 8 + 0], sa, sb), fmaf(f[q * 8 + 1], sa, sb));
+        o.y = pack_half2(fmaf(f[q * 8 + 2], sa, sb), fmaf(f[q * 8 + 3], sa, sb));
+        o.z = pack_half2(fmaf(f[q * 8 + 4], sa, sb), fmaf(f[q * 8 + 5], sa, sb));
+        o.w = pack_half2(fmaf(f[q * 8 + 6], sa, sb), fmaf(f[q * 8 + 7], sa, sb));
         *reinterpret_cast<uint4*>(zt + sw128_off(row, q)) = o;
       }
       fence_proxy_async_smem();

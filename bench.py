@@ -69,16 +69,56 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled DURING the timed region.
+
+    NVML is read from a background thread every 10 ms (read-only queries; nothing is set),
+    so even a timed region of a few tens of milliseconds gets samples; nvidia-smi's
+    200 ms loop is the fallback when NVML is unavailable. `index` is the CUDA device
+    ordinal of this process; the NVML handle is found by the device's UUID so that
+    CUDA_VISIBLE_DEVICES remapping cannot pick the wrong GPU."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.01
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.thread = None
+        self.samples = []          # (sm_mhz, max_mhz, reasons bitmask)
+        self.lines = []
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid if not uuid.startswith("GPU-") else uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx,
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    self._stop.wait(self.PERIOD_S)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
@@ -89,7 +129,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -100,10 +142,20 @@ class ClockSampler:
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
         return False
 
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
+
     def summary(self):
         sm, mx, reasons = [], None, set()
+        for clk, mxc, bits in self.samples:
+            sm.append(float(clk))
+            mx = float(mxc)
+            for name, bit in self.REASON_BITS.items():
+                if bits & bit:
+                    reasons.add(name)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -119,7 +171,8 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
         loaded = [x for x in sm if x > 0.5 * max(sm)] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 # --------------------------------------------------------------------------- reference

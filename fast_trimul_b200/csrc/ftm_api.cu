@@ -122,6 +122,17 @@ bool make_z_map(CUtensorMap* m, const ftm_problem* p, const void* z, bool transp
 
 // FTM_TEST_STALL=input makes the input stage withhold one tile load so its bounded
 // waits expire: the failure-detection test of the device error path (no fault, no trap)
+// L2 prefetch distance of a stage's producers in tiles: FTM_PREFETCH_IN / FTM_PREFETCH_OUT
+// (or FTM_PREFETCH for both); the input stage gains from one tile ahead, the output stage
+// (two streams already in flight per slot) from none
+int prefetch_distance(const char* var, int dflt) {
+  const char* v = getenv(var);
+  if (!v || !*v) v = getenv("FTM_PREFETCH");
+  if (!v || !*v) return dflt;
+  const int d = atoi(v);
+  return d < 0 ? 0 : (d > 8 ? 8 : d);
+}
+
 int test_stall_requested() {
   const char* v = getenv("FTM_TEST_STALL");
   return (v && strcmp(v, "input") == 0) ? 1 : 0;
@@ -131,6 +142,7 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
              void* a_cm, void* b_cm, float* zstats, int* err, cudaStream_t stream, int dev) {
   PosTiling tl;
   tl.init(p->batch, p->rows, p->cols);
+  tl.pf = prefetch_distance("FTM_PREFETCH_IN", 1);
   const bool incoming = p->mode == FTM_INCOMING;
   CUtensorMap zmap, wmap;
   if (!make_z_map(&zmap, p, z, incoming, tl)) return FTM_LAUNCH_FAILED;
@@ -214,6 +226,7 @@ int stage_out(const ftm_problem* p, const void* z, const float* mask, const void
               int dev) {
   PosTiling tl;
   tl.init(p->batch, p->rows, p->cols);
+  tl.pf = prefetch_distance("FTM_PREFETCH_OUT", 0);
   CUtensorMap zmap, xmap, wmap;
   if (!make_z_map(&zmap, p, z, false, tl)) return FTM_LAUNCH_FAILED;
   {

@@ -154,6 +154,16 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// L2 prefetch of a tensor tile (no shared memory, no barrier): starts the HBM read of a
+// tile the producer will load a few iterations later, so more bytes are in flight per SM
+// than the shared-memory ring alone allows
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // TMA tensor stores (shared -> global), bulk-group completion
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1,
                                              int c2, int c3) {
@@ -278,6 +288,13 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[1
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// 32 TMEM lanes x 8 columns, issued without waiting (pair with tmem_wait_ld)
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -399,7 +416,9 @@ struct PosTiling {
   int R, S, B;      // grid rows, columns, batches
   int vt, ut;       // tile shape (vt * ut == 128), vt in {64, 128}
   int tiles_u, tiles_v, tiles;
+  int pf;           // L2 prefetch distance of the stage producers, in own tiles (0: off)
   __host__ __device__ void init(int batch, int rows, int cols) {
+    pf = 0;
     B = batch;
     R = rows;
     S = cols;

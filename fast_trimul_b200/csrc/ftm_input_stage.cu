@@ -103,6 +103,15 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int s = it % kInBufs;
         const uint32_t ph = (it / kInBufs) & 1;
+        for (int d = (it == 0 ? 1 : max(tl.pf, 1)); d <= tl.pf; ++d) {   // keep tl.pf tiles ahead in L2
+          const int tp = t + d * static_cast<int>(gridDim.x);
+          if (tp < ntiles) {
+            int pb, pu, pv;
+            tl.tile(tp, pb, pu, pv);
+            tma_prefetch_l2_4d(&zmap, 0, pv, pu, pb);
+            tma_prefetch_l2_4d(&zmap, 64, pv, pu, pb);
+          }
+        }
         if (!mbar_wait(&buf_empty[s], ph ^ 1, err, err_code(KERNEL_INPUT, ROLE_PRODUCER, 1))) break;
         // failure-detection test: CTA 0 never loads its first tile, so the waits on it
         // must expire, record the error and let every role drain and exit

@@ -139,6 +139,15 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       int it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int s = it % kOutBufs;
+        for (int d = (it == 0 ? 1 : max(tl.pf, 1)); d <= tl.pf; ++d) {   // keep tl.pf tiles ahead in L2
+          const int tp = t + d * static_cast<int>(gridDim.x);
+          if (tp < ntiles) {
+            int pb, pu, pv;
+            tl.tile(tp, pb, pu, pv);
+            for (int h = 0; h < 2; ++h)
+              tma_prefetch_l2_4d(&xmap, tl.vt == 128 ? pv + 64 * h : pv, tl.vt == 128 ? pu : pu + h, 0, pb);
+          }
+        }
         if (!mbar_wait(&x_empty[s], ((it / kOutBufs) & 1) ^ 1, err,
                        err_code(KERNEL_OUTPUT, ROLE_PRODUCER, 1)))
           break;
@@ -160,6 +169,15 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       int it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int s = it % kOutBufs;
+        for (int d = (it == 0 ? 1 : max(tl.pf, 1)); d <= tl.pf; ++d) {
+          const int tp = t + d * static_cast<int>(gridDim.x);
+          if (tp < ntiles) {
+            int pb, pu, pv;
+            tl.tile(tp, pb, pu, pv);
+            tma_prefetch_l2_4d(&zmap, 0, pv, pu, pb);
+            tma_prefetch_l2_4d(&zmap, 64, pv, pu, pb);
+          }
+        }
         if (!mbar_wait(&z_empty[s], ((it / kOutBufs) & 1) ^ 1, err,
                        err_code(KERNEL_OUTPUT, ROLE_PRODUCER, 2)))
           break;

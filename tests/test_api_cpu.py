@@ -257,3 +257,18 @@ def test_c_abi_exports_every_declared_symbol():
     _lib.load()
     assert _lib.status_string(0) == "ok"
     assert set(_lib.SIGNATURES) <= declared
+
+
+def test_clock_sampler_summary_reads_nvml_reason_bits():
+    """The bench's clock record: median SM clock under load and the NVML clock-event
+    reasons seen during the timed region (sw_power_cap kept, slowdowns reported)."""
+    import sys, os
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from bench import ClockSampler
+    c = ClockSampler(0)
+    c.samples = [(1965, 1965, 0x0), (1900, 1965, 0x4), (345, 1965, 0x1), (1930, 1965, 0x4 | 0x40)]
+    s = c.summary()
+    assert s["samples"] == 4 and s["sm_max_mhz"] == 1965.0
+    assert s["sm_mhz"] == 1930.0                       # idle sample (345) left out
+    assert s["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
+    assert ClockSampler(0).summary()["samples"] == 0

@@ -418,6 +418,66 @@ def bench_sweep(args, torch, layer, dev):
     return rows
 
 
+def contraction_vs_cublas(ns, launches=150):
+    """The contraction kernel alone against cuBLAS (torch.bmm) on the same batched problem
+    X[l] = A[l] B[l]^T, 128 channels of N x N x N, fp16 operands, fp32 accumulation.
+    Short runs: median of 10 back-to-back launches (CUDA events). Sustained runs:
+    `launches` back-to-back launches with NVML energy and SM clocks sampled during them
+    (both kernels hit the 1 kW power cap; energy per launch decides the clock)."""
+    import time
+    import torch
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    s = torch.cuda.current_stream().cuda_stream
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(0).uuid))
+    except Exception:
+        h = None
+    for n in ns:
+        L = C
+        A = torch.randn(L, n, n, device="cuda").half()
+        B = torch.randn(L, n, n, device="cuda").half()
+        X = torch.empty(L, n, n, device="cuda", dtype=torch.half)
+        err = torch.zeros(64, dtype=torch.int32, device="cuda")
+        kernels = {
+            "ftm_contraction": lambda: lib.ftm_contraction(A.data_ptr(), B.data_ptr(), X.data_ptr(), L, n,
+                                                           n, n, 1, err.data_ptr(), s),
+            "cublas_bmm": lambda: torch.bmm(A, B.transpose(1, 2), out=X),
+        }
+        flops = 2 * L * n ** 3
+        for name, f in kernels.items():
+            for _ in range(5):
+                f()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(11)]
+            ev[0].record()
+            for i in range(10):
+                f()
+                ev[i + 1].record()
+            torch.cuda.synchronize()
+            short = statistics.median(ev[i].elapsed_time(ev[i + 1]) for i in range(10))
+            time.sleep(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            j0 = pynvml.nvmlDeviceGetTotalEnergyConsumption(h) if h is not None else None
+            with ClockSampler(0) as clk:
+                e0.record()
+                for _ in range(launches):
+                    f()
+                e1.record()
+                torch.cuda.synchronize()
+            j1 = pynvml.nvmlDeviceGetTotalEnergyConsumption(h) if h is not None else None
+            sus = e0.elapsed_time(e1) / launches
+            lib.ftm_check_error(err.data_ptr(), None, s)
+            print(json.dumps({"kernel": name, "n": n, "short_ms": round(short, 4),
+                              "short_tflops": round(flops / short / 1e9, 1),
+                              "sustained_ms": round(sus, 4),
+                              "sustained_tflops": round(flops / sus / 1e9, 1),
+                              "joules_per_launch": None if j0 is None else round((j1 - j0) / 1e3 / launches, 3),
+                              "clocks": clk.summary()}))
+        del A, B, X
+
+
 def reference_gpu_sweep(ns):
     """The reference's own FastTriangleMultiplication (its CuTe-DSL Ampere kernels, fp16)
     on this GPU, imported from baseline/_ref (the reference's pure-Python package;
@@ -543,12 +603,18 @@ def main():
     ap.add_argument("--reference-gpu-sweep", type=int, nargs="*", default=None, metavar="N",
                     help="time the reference's own GPU kernels (baseline/_ref, CUDA-graphed) at "
                          "these N and print one JSON line each")
+    ap.add_argument("--contraction-vs-cublas", type=int, nargs="*", default=None, metavar="N",
+                    help="time the contraction kernel alone against cuBLAS bmm (short and "
+                         "sustained, with energy and clocks) at these N and exit")
     ap.add_argument("--profile-shard", type=int, default=0, metavar="P",
                     help="with --profile-case: run one rank's kernels of the P-way channel-sharded "
                          "forward on this GPU (no communication)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
+        return
+    if args.contraction_vs_cublas is not None:
+        contraction_vs_cublas(args.contraction_vs_cublas or [1024, 2048])
         return
     if args.reference_gpu_sweep is not None:
         reference_gpu_sweep(args.reference_gpu_sweep or [256, 512, 1024, 2048])

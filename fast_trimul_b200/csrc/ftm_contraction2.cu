@@ -23,16 +23,27 @@ namespace ftm {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;   // per-CTA halves of the 256 x 256 tile
-constexpr int kStages = 6;
+constexpr int kBM = 128, kBN = 128, kBK = 64;   // per-CTA halves of one 256 x 256 MMA tile
 constexpr int kATile = kBM * kBK * 2;          // 16 KB
 constexpr int kBTile = kBN * kBK * 2;          // 16 KB
-constexpr int kStageBytes = kATile + kBTile;
-constexpr int kOffBar = kStages * kStageBytes;
-constexpr int kNumBars = 2 * kStages + 4 + 1;
-constexpr int kOffTmem = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffTmem + 16 + 1024;
 constexpr int kThreads = 192;
+
+// NH = number of 256-wide N halves per pair tile: NH = 1 gives 256 x 256 tiles with two
+// 256-column TMEM accumulators (the epilogue of one tile overlaps the next tile's MMAs);
+// NH = 2 gives 256 x 512 tiles whose two N halves share each A stage (a third less
+// operand traffic per FLOP from L2) in one 512-column accumulator.
+template <int NH>
+struct PairCfg {
+  static constexpr int kStages = NH == 1 ? 6 : 4;
+  static constexpr int kStageBytes = kATile + NH * kBTile;
+  static constexpr int kAcc = NH == 1 ? 2 : 1;          // accumulators in TMEM
+  static constexpr int kAccCols = 256 * NH;             // columns per accumulator
+  static constexpr int kOffBar = kStages * kStageBytes;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAcc + 1;
+  static constexpr int kOffTmem = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffTmem + 16 + 1024;
+  static_assert(kSmemBytes <= 232448, "pair contraction exceeds 227 KB of shared memory");
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -86,21 +97,25 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cl) {
                : "memory");
 }
 
+template <int NH>
 __global__ void __launch_bounds__(kThreads, 1)
 contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
                         const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
                         int M, int N, int K, int rows_per_block, int a_rows_per_block,
                         int* err) {
+  using Cfg = PairCfg<NH>;
+  constexpr int kStages = Cfg::kStages, kStageBytes = Cfg::kStageBytes, kAcc = Cfg::kAcc;
+  constexpr int kAccCols = Cfg::kAccCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* full = bars;                  // leader: operands of both CTAs landed
   uint64_t* empty = bars + kStages;       // both: stage consumed by the pair MMA
   uint64_t* tmem_full = bars + 2 * kStages;
-  uint64_t* tmem_empty = tmem_full + 2;   // leader: 4 local + 4 peer epilogue warps
-  uint64_t* mma_drain = tmem_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  uint64_t* tmem_empty = tmem_full + kAcc;   // leader: 4 local + 4 peer epilogue warps
+  uint64_t* mma_drain = tmem_empty + kAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffTmem);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -112,7 +127,7 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAcc; ++a) {
       mbar_init(&tmem_full[a], 1);
       mbar_init(&tmem_empty[a], 8);
     }
@@ -132,7 +147,7 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
   const uint32_t tmem_base = *tmem_slot;
 
   const int tiles_m = (M + 2 * kBM - 1) / (2 * kBM);
-  const int tiles_n = (N + 2 * kBN - 1) / (2 * kBN);
+  const int tiles_n = (N + 2 * kBN * NH - 1) / (2 * kBN * NH);
   const int per_l = tiles_m * tiles_n;
   const int ntiles = L * per_l;
   const int nk = (K + kBK - 1) / kBK;
@@ -154,8 +169,13 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
         const int i0 = tm * 2 * kBM + static_cast<int>(rank) * kBM;
         const int ablk = i0 / a_rows_per_block, ail = i0 - ablk * a_rows_per_block;
-        const int j0 = tn * 2 * kBN + static_cast<int>(rank) * kBN;
-        const int blk = j0 / rows_per_block, jl = j0 - blk * rows_per_block;
+        int bblk[NH], bjl[NH];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          const int j0 = (tn * NH + h) * 2 * kBN + static_cast<int>(rank) * kBN;
+          bblk[h] = j0 / rows_per_block;
+          bjl[h] = j0 - bblk[h] * rows_per_block;
+        }
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[st], ph ^ 1, err, err_code(KERNEL_CONTRACT, ROLE_PRODUCER, 2))) {
             ok = false;
@@ -165,7 +185,9 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
           const uint32_t fb = cluster_addr(&full[st], 0);
           if (leader) mbar_arrive_expect_tx(&full[st], 2 * kStageBytes);
           tma_load_4d_pair(&amap, fb, sa, kb * kBK, ail, l, ablk);
-          tma_load_4d_pair(&bmap, fb, sa + kATile, kb * kBK, jl, l, blk);
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+            tma_load_4d_pair(&bmap, fb, sa + kATile + h * kBTile, kb * kBK, bjl[h], l, bblk[h]);
           ++issued;
           if (++st == kStages) {
             st = 0;
@@ -189,14 +211,14 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
       int it = 0;
       bool ok = true;
       for (int t = cid; ok && t < ntiles; t += ncl, ++it) {
-        const int acc = it & 1;
-        if (!mbar_wait(&tmem_empty[acc], ((it >> 1) & 1) ^ 1, err,
+        const int acc = it % kAcc;
+        if (!mbar_wait(&tmem_empty[acc], ((it / kAcc) & 1) ^ 1, err,
                        err_code(KERNEL_CONTRACT, ROLE_MMA, 4))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * (2 * kBN);
+        const uint32_t d = tmem_base + acc * kAccCols;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[st], ph, err, err_code(KERNEL_CONTRACT, ROLE_MMA, 5))) {
             ok = false;
@@ -207,8 +229,11 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t ad = kmajor_desc(sa + kk * 32);
-            const uint64_t bd = kmajor_desc(sa + kATile + kk * 32);
-            umma_f16_pair(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+              const uint64_t bd = kmajor_desc(sa + kATile + h * kBTile + kk * 32);
+              umma_f16_pair(d + h * 256, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
           umma_commit_pair(cluster_addr(&empty[st], 0));
           umma_commit_pair(cluster_addr(&empty[st], 1));
@@ -230,11 +255,11 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(sub * 32) << 16);
     int it = 0;
     for (int t = cid; t < ntiles; t += ncl, ++it) {
-      const int acc = it & 1;
+      const int acc = it % kAcc;
       const int l = t / per_l;
       const int r = t - l * per_l;
       const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
-      if (!mbar_wait_warp(&tmem_full[acc], (it >> 1) & 1, err,
+      if (!mbar_wait_warp(&tmem_full[acc], (it / kAcc) & 1, err,
                           err_code(KERNEL_CONTRACT, ROLE_EPILOGUE, 2)))
         break;
       tc_fence_after();
@@ -242,25 +267,30 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
       // X rows are stored in blocks of a_rows_per_block like A: [block][l][row][col]
       const int xb = i / a_rows_per_block, xi = i - xb * a_rows_per_block;
       __half* xrow = X + ((static_cast<size_t>(xb) * L + l) * a_rows_per_block + xi) * N;
+      // 16-column chunks, the TMEM load of chunk ch + 1 in flight while chunk ch is
+      // converted and stored
       uint32_t va[2][16];
-#pragma unroll 1
-      for (int ch = 0; ch < (2 * kBN) / 16; ++ch) {
-        tmem_ld16_nowait(lane_base + acc * (2 * kBN) + ch * 16, va[0]);
-        tmem_wait_ld();
-        const int j = tn * 2 * kBN + ch * 16;
+      tmem_ld16_nowait(lane_base + acc * kAccCols, va[0]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int ch = 0; ch < kAccCols / 16; ++ch) {
+        const int cur = ch & 1;
+        if (ch + 1 < kAccCols / 16) tmem_ld16_nowait(lane_base + acc * kAccCols + (ch + 1) * 16, va[cur ^ 1]);
+        const int j = tn * kAccCols + ch * 16;
         if (i < M) {
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             if (j + q * 8 < N) {
               uint4 o;
-              o.x = pack_half2(__uint_as_float(va[0][q * 8 + 0]), __uint_as_float(va[0][q * 8 + 1]));
-              o.y = pack_half2(__uint_as_float(va[0][q * 8 + 2]), __uint_as_float(va[0][q * 8 + 3]));
-              o.z = pack_half2(__uint_as_float(va[0][q * 8 + 4]), __uint_as_float(va[0][q * 8 + 5]));
-              o.w = pack_half2(__uint_as_float(va[0][q * 8 + 6]), __uint_as_float(va[0][q * 8 + 7]));
+              o.x = pack_half2(__uint_as_float(va[cur][q * 8 + 0]), __uint_as_float(va[cur][q * 8 + 1]));
+              o.y = pack_half2(__uint_as_float(va[cur][q * 8 + 2]), __uint_as_float(va[cur][q * 8 + 3]));
+              o.z = pack_half2(__uint_as_float(va[cur][q * 8 + 4]), __uint_as_float(va[cur][q * 8 + 5]));
+              o.w = pack_half2(__uint_as_float(va[cur][q * 8 + 6]), __uint_as_float(va[cur][q * 8 + 7]));
               *reinterpret_cast<uint4*>(xrow + j + q * 8) = o;
             }
           }
         }
+        if (ch + 1 < kAccCols / 16) tmem_wait_ld();
       }
       tc_fence_before();
       __syncwarp();
@@ -293,27 +323,33 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
                                     int L, int M, int N, int K, int rows_per_block,
                                     int a_rows_per_block, int* err,
                                     int num_sms, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(contraction_pair_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e != cudaSuccess) return e;
-  const long tiles = long(L) * ((M + 255) / 256) * ((N + 255) / 256);
-  const int clusters = static_cast<int>(tiles < num_sms / 2 ? tiles : num_sms / 2);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, contraction_pair_kernel, amap, bmap, X, L, M, N, K, rows_per_block,
-                         a_rows_per_block, err);
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
+  // FTM_CT_NH=2 selects the 256 x 512 tile variant
+  const char* nh_env = getenv("FTM_CT_NH");
+  const int nh = (nh_env && atoi(nh_env) == 2) ? 2 : 1;
+  auto go = [&](auto kern, int smem_bytes, int tile_n) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    const long tiles = long(L) * ((M + 255) / 256) * ((N + tile_n - 1) / tile_n);
+    const int clusters = static_cast<int>(tiles < num_sms / 2 ? tiles : num_sms / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, amap, bmap, X, L, M, N, K, rows_per_block,
+                           a_rows_per_block, err);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  };
+  if (nh == 2) return go(contraction_pair_kernel<2>, PairCfg<2>::kSmemBytes, 512);
+  return go(contraction_pair_kernel<1>, PairCfg<1>::kSmemBytes, 256);
 }
 
 }  // namespace ftm

@@ -107,13 +107,19 @@ def test_golden_fixtures_d128():
         assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (f, max_abs, mean_rel)
 
 
+def _select_contraction(kernel, monkeypatch):
+    """pair: 256 x 256 CTA-pair tiles; pair_wide: 256 x 512 (FTM_CT_NH=2); single: 128 x 256."""
+    monkeypatch.setenv("FTM_CONTRACTION", "single" if kernel == "single" else "pair")
+    monkeypatch.setenv("FTM_CT_NH", "2" if kernel == "pair_wide" else "1")
+
+
 @needs_gpu
-@pytest.mark.parametrize("kernel", ["pair", "single"])
+@pytest.mark.parametrize("kernel", ["pair", "pair_wide", "single"])
 @pytest.mark.parametrize("L,m,n,k", [(3, 64, 64, 64), (2, 200, 136, 72), (4, 256, 512, 1024),
                                      (1, 1024, 1024, 1024), (2, 8, 8, 8), (3, 384, 640, 200)])
 def test_contraction_vs_matmul(L, m, n, k, kernel, monkeypatch):
-    monkeypatch.setenv("FTM_CONTRACTION", kernel)
     """ftm_contraction alone against an fp32 matmul of the same fp16 operands."""
+    _select_contraction(kernel, monkeypatch)
     from fast_trimul_b200 import _lib
     lib = _lib.load()
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -132,10 +138,10 @@ def test_contraction_vs_matmul(L, m, n, k, kernel, monkeypatch):
 
 
 @needs_gpu
-@pytest.mark.parametrize("kernel", ["pair", "single"])
+@pytest.mark.parametrize("kernel", ["pair", "pair_wide", "single"])
 def test_contraction_blocked_b(kernel, monkeypatch):
     """B given as row blocks (the layout an all-gather of row shards produces)."""
-    monkeypatch.setenv("FTM_CONTRACTION", kernel)
+    _select_contraction(kernel, monkeypatch)
     from fast_trimul_b200 import _lib
     lib = _lib.load()
     L, m, k, rpb, blocks = 3, 256, 512, 256, 2

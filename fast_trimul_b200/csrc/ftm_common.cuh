@@ -401,6 +401,12 @@ __device__ __forceinline__ float gated_tanh_half(float hp, float hg) {
   return fmaf(hp, tanh_mufu(hg), hp);
 }
 
+// two lanes of the same at once: FFMA2 (sm_100 packed fp32, IEEE round-to-nearest per
+// lane) for the affine part, two MUFU tanh
+__device__ __forceinline__ float2 gated_tanh_half2(float2 hp, float2 hg) {
+  return __ffma2_rn(hp, make_float2(tanh_mufu(hg.x), tanh_mufu(hg.y)), hp);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -210,30 +210,39 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[q * 8 + e] = t8[e];
       }
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // packed fp32x2 arithmetic (FADD2 / FFMA2): eight partial sums in four pairs
+      float2 ps[4];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) ps[i & 7] += f[i];
-      float tot = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      for (int e = 0; e < 4; ++e) ps[e] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) ps[i & 3] = __fadd2_rn(ps[i & 3], make_float2(f[2 * i], f[2 * i + 1]));
+      float tot = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
       tot += __shfl_xor_sync(0xffffffffu, tot, 16);
       const float mean = tot * (1.0f / kC);
+      const float2 nmean = make_float2(-mean, -mean);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+      for (int e = 0; e < 4; ++e) ps[e] = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) ps[i & 7] = fmaf(f[i] - mean, f[i] - mean, ps[i & 7]);
-      float sq = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      for (int i = 0; i < 32; ++i) {
+        const float2 d = __fadd2_rn(make_float2(f[2 * i], f[2 * i + 1]), nmean);
+        ps[i & 3] = __ffma2_rn(d, d, ps[i & 3]);
+      }
+      float sq = ((ps[0].x + ps[0].y) + (ps[1].x + ps[1].y)) + ((ps[2].x + ps[2].y) + (ps[3].x + ps[3].y));
       sq += __shfl_xor_sync(0xffffffffu, sq, 16);
       const float var = sq * (1.0f / kC);
       const float sa = m * rsqrtf(m * m * var + eps);
       const float sb = -mean * sa;
       if (valid && half == 0) zstats[zi] = make_float2(mean, sa);   // reused by the output stage
+      const float2 sa2 = make_float2(sa, sa), sb2 = make_float2(sb, sb);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        uint4 o;
-        o.x = pack_half2(fmaf(f[q * 8 + 0], sa, sb), fmaf(f[q * 8 + 1], sa, sb));
-        o.y = pack_half2(fmaf(f[q * 8 + 2], sa, sb), fmaf(f[q * 8 + 3], sa, sb));
-        o.z = pack_half2(fmaf(f[q * 8 + 4], sa, sb), fmaf(f[q * 8 + 5], sa, sb));
-        o.w = pack_half2(fmaf(f[q * 8 + 6], sa, sb), fmaf(f[q * 8 + 7], sa, sb));
-        *reinterpret_cast<uint4*>(zt + sw128_off(row, q)) = o;
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 y = __ffma2_rn(make_float2(f[q * 8 + 2 * e], f[q * 8 + 2 * e + 1]), sa2, sb2);
+          o[e] = pack_half2(y.x, y.y);
+        }
+        *reinterpret_cast<uint4*>(zt + sw128_off(row, q)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&a_ready[s]);
@@ -276,11 +285,14 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           float p[32], g[32];
           tmem_ld32x2(lane_base + h * 256 + p0, lane_base + h * 256 + 128 + p0, p, g);
           uint32_t packed[16];
+          const float2 half2f = make_float2(0.5f, 0.5f);
+          const float2 vp2 = make_float2(vp[h], vp[h]), vg2 = make_float2(vg[h], vg[h]);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            packed[i / 2] = pack_half2(gated_tanh_half(fmaf(0.5f, p[i], vp[h]), fmaf(0.5f, g[i], vg[h])),
-                                       gated_tanh_half(fmaf(0.5f, p[i + 1], vp[h]),
-                                                       fmaf(0.5f, g[i + 1], vg[h])));
+          for (int i = 0; i < 32; i += 2) {
+            const float2 a2 = gated_tanh_half2(__ffma2_rn(half2f, make_float2(p[i], p[i + 1]), vp2),
+                                               __ffma2_rn(half2f, make_float2(g[i], g[i + 1]), vg2));
+            packed[i / 2] = pack_half2(a2.x, a2.y);
+          }
           // staging row = channel, 64 positions (128 B, 128-byte swizzle)
 #pragma unroll
           for (int q = 0; q < 4; ++q)

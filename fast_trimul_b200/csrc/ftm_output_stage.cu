@@ -86,7 +86,8 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   uint8_t* sSlots = smem + kOffSlots;
   float4* sStats = reinterpret_cast<float4*>(smem + kOffStats);
   float* sMask = reinterpret_cast<float*>(smem + kOffMask);
-  // per channel {u_g/2, v_g/2, u_o, v_o} (gate constants halved for the tanh form)
+  // per channel pair (2k, 2k+1): {u_g/2 x2, v_g/2 x2}, {u_o x2, v_o x2} -- gate constants
+  // halved for the tanh form, laid out as float2 pairs for the packed fp32x2 epilogue
   float4* sUV = reinterpret_cast<float4*>(smem + kOffUV);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* w_full = bars;
@@ -119,8 +120,10 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < kC; i += blockDim.x)
-    sUV[i] = make_float4(0.5f * u_g[i], 0.5f * v_g[i], u_o[i], v_o[i]);
+  for (int k = threadIdx.x; k < kC / 2; k += blockDim.x) {
+    sUV[2 * k] = make_float4(0.5f * u_g[2 * k], 0.5f * u_g[2 * k + 1], 0.5f * v_g[2 * k], 0.5f * v_g[2 * k + 1]);
+    sUV[2 * k + 1] = make_float4(u_o[2 * k], u_o[2 * k + 1], v_o[2 * k], v_o[2 * k + 1]);
+  }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -257,19 +260,24 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const int h = row >> 6, e = row & 63;
       const uint8_t* xcol = xs + h * kHalfTile + (e & 7) * 2;
       const float xshift = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(0, e >> 3)));
-      float a1[4] = {0.f, 0.f, 0.f, 0.f}, a2[4] = {0.f, 0.f, 0.f, 0.f};
+      // channel pairs in packed fp32x2 (FADD2 / FFMA2): eight partial sums in four pairs
+      float2 a1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      float2 a2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 nshift = make_float2(-xshift, -xshift);
 #pragma unroll 8
       for (int c = 0; c < kC; c += 4) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float d = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c + k, e >> 3))) - xshift;
-          a1[k] += d;
-          a2[k] = fmaf(d, d, a2[k]);
+        for (int k = 0; k < 2; ++k) {
+          const float x0 = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c + 2 * k, e >> 3)));
+          const float x1 = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c + 2 * k + 1, e >> 3)));
+          const float2 d = __fadd2_rn(make_float2(x0, x1), nshift);
+          a1[k] = __fadd2_rn(a1[k], d);
+          a2[k] = __ffma2_rn(d, d, a2[k]);
         }
       }
-      dm = ((a1[0] + a1[1]) + (a1[2] + a1[3])) * inv_c;
+      dm = ((a1[0].x + a1[0].y) + (a1[1].x + a1[1].y)) * inv_c;
       const float mean_x = xshift + dm;
-      const float var_x = fmaxf(((a2[0] + a2[1]) + (a2[2] + a2[3])) * inv_c - dm * dm, 0.f);
+      const float var_x = fmaxf(((a2[0].x + a2[0].y) + (a2[1].x + a2[1].y)) * inv_c - dm * dm, 0.f);
       if (!mbar_wait(&full_z[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 2)))
         break;
       if (z_bf16) {   // bf16 -> fp16 in place (exact inside fp16 range): the MMA operand
@@ -311,6 +319,9 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const float4 st = sStats[(it % kStatRing) * 128 + row];
       const float m = sMask[(it % kStatRing) * 128 + row];
       const float hm = 0.5f * m, m2 = m * m;
+      const float2 hm2 = make_float2(hm, hm), m22 = make_float2(m2, m2);
+      const float2 stx2 = make_float2(st.x, st.x), sty2 = make_float2(st.y, st.y);
+      const float2 stz2 = make_float2(st.z, st.z), stw2 = make_float2(st.w, st.w);
       uint8_t* zs = sSlots + s * kSlot;
       // four 16-column sub-chunks per warp; the TMEM load of sub-chunk k+1 is in
       // flight while sub-chunk k is computed
@@ -338,12 +349,20 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         }
         float r[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          // out = m^2 z (residual) + m * o * sigmoid(g), sigmoid(g) = (1 + tanh(g/2)) / 2
-          const float4 uv = sUV[n0 + i];
-          const float hmo = hm * fmaf(st.z, __uint_as_float(orr[cur][i]), fmaf(st.w, uv.z, uv.w));
-          const float t = tanh_mufu(fmaf(st.x, __uint_as_float(gr[cur][i]), fmaf(st.y, uv.x, uv.y)));
-          r[i] = fmaf(hmo, t, residual ? fmaf(m2, zv[i], hmo) : hmo);
+        for (int i = 0; i < 16; i += 2) {
+          // out = m^2 z (residual) + m * o * sigmoid(g), sigmoid(g) = (1 + tanh(g/2)) / 2,
+          // two channels per packed fp32x2 operation
+          const float4 cg = sUV[n0 + i], co = sUV[n0 + i + 1];
+          const float2 to = __ffma2_rn(stz2, make_float2(__uint_as_float(orr[cur][i]), __uint_as_float(orr[cur][i + 1])),
+                                       __ffma2_rn(stw2, make_float2(co.x, co.y), make_float2(co.z, co.w)));
+          const float2 hmo = __fmul2_rn(hm2, to);
+          const float2 tg = __ffma2_rn(stx2, make_float2(__uint_as_float(gr[cur][i]), __uint_as_float(gr[cur][i + 1])),
+                                       __ffma2_rn(sty2, make_float2(cg.x, cg.y), make_float2(cg.z, cg.w)));
+          const float2 th = make_float2(tanh_mufu(tg.x), tanh_mufu(tg.y));
+          const float2 base = residual ? __ffma2_rn(m22, make_float2(zv[i], zv[i + 1]), hmo) : hmo;
+          const float2 rr = __ffma2_rn(hmo, th, base);
+          r[i] = rr.x;
+          r[i + 1] = rr.y;
         }
         if (OUT_DT == 0) {
           if (valid) {

@@ -595,7 +595,7 @@ def main():
     ap.add_argument("--no-trunk", action="store_true")
     ap.add_argument("--chunks", type=int, default=None,
                     help="channel chunks of the exchange (N>1; default 4 for all-gather, 2 for all-to-all)")
-    ap.add_argument("--scheme", default=None, choices=["allgather", "alltoall", "allgather_ce", "alltoall_ce"],
+    ap.add_argument("--scheme", default=None, choices=["allgather", "alltoall", "allgather_ce", "alltoall_ce", "fused"],
                     help="multi-GPU exchange (default: allgather_ce for 2 GPUs, alltoall_ce for more)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="N",
                     help="run a few plain forwards at this N (for ncu captures) and exit")

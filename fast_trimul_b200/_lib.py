@@ -31,8 +31,25 @@ class Problem(ctypes.Structure):
                 ("eps_in", ctypes.c_float), ("eps_out", ctypes.c_float)]
 
 
+MAX_RANKS = 8
+
+
+class PeerPlanes(ctypes.Structure):
+    """Mirror of ftm_peer_planes: rank q's receive plane as mapped in this process."""
+    _fields_ = [("world", _i32), ("rank", _i32), ("base", _vp * MAX_RANKS)]
+
+    @classmethod
+    def make(cls, world, rank, ptrs):
+        pp = cls()
+        pp.world, pp.rank = world, rank
+        for q, ptr in enumerate(ptrs):
+            pp.base[q] = ptr
+        return pp
+
+
 _PP = ctypes.POINTER(Problem)
 _IP = ctypes.POINTER(ctypes.c_int)
+_PPL = ctypes.POINTER(PeerPlanes)
 
 SIGNATURES = {
     "ftm_packed_params_bytes": (_sz, [_i32, _i32]),
@@ -44,6 +61,8 @@ SIGNATURES = {
     "ftm_contraction_blocked": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
                                                _vp, _vp]),
     "ftm_output_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_input_stage_scatter": (ctypes.c_int, [_PP, _vp, _vp, _vp, _PPL, _PPL, _vp, _vp, _vp]),
+    "ftm_contraction_scatter": (ctypes.c_int, [_vp, _vp, _PPL, _i32, _i32, _i32, _i32, _vp, _vp]),
     "ftm_check_error": (ctypes.c_int, [_vp, _IP, _vp]),
     "ftm_workspace_error_word": (_vp, [_PP, _vp]),
     "ftm_status_string": (ctypes.c_char_p, [ctypes.c_int]),

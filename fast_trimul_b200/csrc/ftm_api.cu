@@ -138,8 +138,12 @@ int test_stall_requested() {
   return (v && strcmp(v, "input") == 0) ? 1 : 0;
 }
 
+// a_dst / b_dst null: a and b go to the local channel planes a_cm / b_cm (S, R, C, B).
+// Otherwise each channel group goes to its owner rank's receive plane (see
+// ftm_input_stage_scatter), one tensor map per destination.
 int stage_in(const ftm_problem* p, const void* z, const float* mask, const void* packed,
-             void* a_cm, void* b_cm, float* zstats, int* err, cudaStream_t stream, int dev) {
+             void* a_cm, void* b_cm, float* zstats, int* err, cudaStream_t stream, int dev,
+             const ftm_peer_planes* a_dst = nullptr, const ftm_peer_planes* b_dst = nullptr) {
   PosTiling tl;
   tl.init(p->batch, p->rows, p->cols);
   tl.pf = prefetch_distance("FTM_PREFETCH_IN", 1);
@@ -154,23 +158,41 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
     if (!make_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, pk + L.w_in, dims, strides, box))
       return FTM_LAUNCH_FAILED;
   }
-  // channel-major outputs (S, R, C, B): stores of [32 channel x 64 position] blocks
-  CUtensorMap amap, bmap;
-  {
-    const uint64_t R = p->rows, S = p->cols;
-    const uint64_t dims[4] = {S, R, uint64_t(kC), uint64_t(p->batch)};
+  // channel-major outputs: stores of [box_c channel x 64 position] blocks
+  StoreMaps sm{};
+  const uint64_t R = p->rows, S = p->cols, B = p->batch;
+  if (!a_dst) {
+    sm.lq = kC;
+    sm.box_c = 32;
+    sm.blk_base = 0;
+    sm.sys_fence = 0;
+    const uint64_t dims[4] = {S, R, uint64_t(kC), B};
     const uint64_t strides[3] = {S * 2, R * S * 2, uint64_t(kC) * R * S * 2};
     const uint32_t box[4] = {64, 1, 32, 1};
-    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, a_cm, dims, strides, box) ||
-        !make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, b_cm, dims, strides, box))
+    if (!make_map(&sm.a[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, a_cm, dims, strides, box) ||
+        !make_map(&sm.b[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, b_cm, dims, strides, box))
       return FTM_LAUNCH_FAILED;
+  } else {
+    // receive plane of rank q: [source rank][batch][lq][rows][cols]
+    const int P = a_dst->world, lq = kC / P;
+    sm.lq = lq;
+    sm.box_c = lq < 32 ? lq : 32;
+    sm.blk_base = a_dst->rank * p->batch;
+    sm.sys_fence = 1;
+    const uint64_t dims[4] = {S, R, uint64_t(lq), uint64_t(P) * B};
+    const uint64_t strides[3] = {S * 2, R * S * 2, uint64_t(lq) * R * S * 2};
+    const uint32_t box[4] = {64, 1, uint32_t(sm.box_c), 1};
+    for (int q = 0; q < P; ++q)
+      if (!make_map(&sm.a[q], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, a_dst->base[q], dims, strides, box) ||
+          !make_map(&sm.b[q], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, b_dst->base[q], dims, strides, box))
+        return FTM_LAUNCH_FAILED;
   }
   const int grid = tl.tiles < sm_count(dev) ? tl.tiles : sm_count(dev);
   cudaError_t e = launch_input_stage(
-      zmap, wmap, amap, bmap, mask, reinterpret_cast<const float*>(pk + L.u_in),
-      reinterpret_cast<const float*>(pk + L.v_in), static_cast<__half*>(a_cm),
-      static_cast<__half*>(b_cm), reinterpret_cast<float2*>(zstats), tl, incoming ? 1 : 0,
-      p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, err, grid, stream, test_stall_requested());
+      zmap, wmap, sm, mask, reinterpret_cast<const float*>(pk + L.u_in),
+      reinterpret_cast<const float*>(pk + L.v_in), reinterpret_cast<float2*>(zstats), tl,
+      incoming ? 1 : 0, p->z_dtype == FTM_BF16 ? 1 : 0, p->eps_in, err, grid, stream,
+      test_stall_requested());
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 
@@ -182,8 +204,9 @@ bool use_pair_contraction() {
 }
 
 int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int a_blocks, int k,
-                   int rpb, int blocks, int* err, cudaStream_t stream, int dev) {
-  const bool pair = use_pair_contraction() || a_blocks > 1;
+                   int rpb, int blocks, int* err, cudaStream_t stream, int dev,
+                   const XDest* xdest = nullptr) {
+  const bool pair = use_pair_contraction() || a_blocks > 1 || xdest != nullptr;
   const int m = a_rpb * a_blocks;
   CUtensorMap amap, bmap;
   if (pair) {
@@ -212,7 +235,7 @@ int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int 
   cudaError_t e;
   if (pair) {
     e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, a_rpb, err,
-                                sm_count(dev), stream);
+                                sm_count(dev), stream, xdest);
   } else {
     const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
     const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
@@ -386,6 +409,60 @@ int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
   if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
   const int st = stage_contract(A, B, X, L, a_rows_per_block, a_blocks, k, b_rows_per_block,
                                 b_blocks, err_word, reinterpret_cast<cudaStream_t>(stream), dev);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+static bool peers_ok(const ftm_peer_planes* d) {
+  if (!d || d->world < 1 || d->world > FTM_MAX_RANKS || d->rank < 0 || d->rank >= d->world)
+    return false;
+  if (kC % d->world != 0 || (kC / d->world) % 16 != 0) return false;
+  for (int q = 0; q < d->world; ++q)
+    if (!d->base[q] || !aligned16(d->base[q])) return false;
+  return true;
+}
+
+int ftm_input_stage_scatter(const ftm_problem* p, const void* z, const float* mask,
+                            const void* packed, const ftm_peer_planes* a_dst,
+                            const ftm_peer_planes* b_dst, float* zstats, int* err_word,
+                            ftm_stream_t stream) {
+  g_last_launches = 0;
+  int st = check_problem(p);
+  if (st != FTM_OK) return st;
+  if (!z || !packed || !zstats || !err_word || !a_dst || !b_dst) return FTM_BAD_ARGUMENT;
+  if (p->mode != FTM_OUTGOING) return FTM_BAD_ARGUMENT;     // rows are sharded in outgoing mode
+  if (!peers_ok(a_dst) || !peers_ok(b_dst) || a_dst->world != b_dst->world ||
+      a_dst->rank != b_dst->rank)
+    return FTM_BAD_ARGUMENT;
+  if (!aligned16(z) || !aligned16(packed) || (mask && !aligned16(mask))) return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  st = stage_in(p, z, mask, packed, nullptr, nullptr, zstats, err_word,
+                reinterpret_cast<cudaStream_t>(stream), dev, a_dst, b_dst);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes* x_dst,
+                            int32_t batch, int32_t c_h, int32_t rows, int32_t n, int* err_word,
+                            ftm_stream_t stream) {
+  g_last_launches = 0;
+  if (!A || !B || !err_word || !x_dst) return FTM_BAD_ARGUMENT;
+  if (c_h != kC || !peers_ok(x_dst)) return FTM_BAD_ARGUMENT;
+  const int P = x_dst->world, lq = kC / P;
+  if (batch < 1 || rows < 1 || n != P * rows || rows % kCtBN != 0) return FTM_BAD_SHAPE;
+  if (!aligned16(A) || !aligned16(B)) return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  XDest xd{};
+  for (int q = 0; q < P; ++q) xd.base[q] = static_cast<__half*>(x_dst->base[q]);
+  xd.enabled = 1;
+  xd.lq = lq;
+  xd.c_total = kC;
+  xd.chan_off = x_dst->rank * lq;
+  // A, B: P row blocks (one per source rank) of (batch * lq, rows, n)
+  const int st = stage_contract(A, B, x_dst->base[x_dst->rank], batch * lq, rows, P, n, rows, P,
+                                err_word, reinterpret_cast<cudaStream_t>(stream), dev, &xd);
   if (st == FTM_OK) g_last_launches = 1;
   return st;
 }

@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
                         const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
                         int M, int N, int K, int rows_per_block, int a_rows_per_block,
-                        int* err) {
+                        int* err, const XDest xd) {
   using Cfg = PairCfg<NH>;
   constexpr int kStages = Cfg::kStages, kStageBytes = Cfg::kStageBytes, kAcc = Cfg::kAcc;
   constexpr int kAccCols = Cfg::kAccCols;
@@ -264,9 +264,14 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         break;
       tc_fence_after();
       const int i = tm * 2 * kBM + static_cast<int>(rank) * kBM + sub * 32 + lane;
-      // X rows are stored in blocks of a_rows_per_block like A: [block][l][row][col]
+      // X rows are stored in blocks of a_rows_per_block like A: [block][l][row][col],
+      // or -- scattered -- each block straight into its owner's channel-major plane
       const int xb = i / a_rows_per_block, xi = i - xb * a_rows_per_block;
-      __half* xrow = X + ((static_cast<size_t>(xb) * L + l) * a_rows_per_block + xi) * N;
+      __half* xrow =
+          xd.enabled
+              ? xd.base[xb] + ((static_cast<size_t>(l / xd.lq) * xd.c_total + xd.chan_off + l % xd.lq) *
+                                   a_rows_per_block + xi) * N
+              : X + ((static_cast<size_t>(xb) * L + l) * a_rows_per_block + xi) * N;
       // 16-column chunks, the TMEM load of chunk ch + 1 in flight while chunk ch is
       // converted and stored
       uint32_t va[2][16];
@@ -299,6 +304,7 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         else remote_arrive(cluster_addr(&tmem_empty[acc], 0));
       }
     }
+    if (xd.enabled) __threadfence_system();   // rows stored into peers' planes
   }
 
   // After a failure the two CTAs may have issued different numbers of loads, and the
@@ -322,7 +328,9 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
                                     int L, int M, int N, int K, int rows_per_block,
                                     int a_rows_per_block, int* err,
-                                    int num_sms, cudaStream_t stream) {
+                                    int num_sms, cudaStream_t stream, const XDest* xdest) {
+  XDest xd{};
+  if (xdest) xd = *xdest;
   // FTM_CT_NH=2 selects the 256 x 512 tile variant
   const char* nh_env = getenv("FTM_CT_NH");
   const int nh = (nh_env && atoi(nh_env) == 2) ? 2 : 1;
@@ -344,7 +352,7 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, amap, bmap, X, L, M, N, K, rows_per_block,
-                           a_rows_per_block, err);
+                           a_rows_per_block, err, xd);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };

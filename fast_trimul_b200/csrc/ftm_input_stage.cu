@@ -18,7 +18,9 @@
 //   warps 10-17 TMEM -> registers (lane = channel, 32 positions per load);
 //               proj = acc + (W beta + b), a = proj_p * sigmoid(proj_g); each warp stages a [32 channel x 32
 //               position] block in shared memory and TMA-stores it into the channel
-//               planes a_cm[b][c][u][v].
+//               planes a_cm[b][c][u][v] -- or, row-sharded over P GPUs, straight into
+//               the receive planes of the ranks that own each channel group (one
+//               tensor map per destination, peer memory over NVLink).
 // The two TMEM slots are independent, so the MMA of tile t+1's a-slot overlaps the
 // epilogue of tile t's b-slot.
 #include "ftm_kernels.h"
@@ -42,11 +44,9 @@ constexpr int kSmemBytes = kOffTmem + 16 + 1024;  // + alignment slack
 __global__ void __launch_bounds__(kInThreads, 1)
 input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
                    const __grid_constant__ CUtensorMap wmap,
-                   const __grid_constant__ CUtensorMap amap,
-                   const __grid_constant__ CUtensorMap bmap, const float* __restrict__ mask,
+                   const __grid_constant__ StoreMaps smaps, const float* __restrict__ mask,
                    const float* __restrict__ /*u_in: unused, rows are pre-normalised*/,
                    const float* __restrict__ v_in,
-                   __half* __restrict__ a_cm, __half* __restrict__ b_cm,
                    float2* __restrict__ zstats, PosTiling tl, int incoming, int z_bf16, float eps,
                    int* err, int test_stall) {
   extern __shared__ uint8_t smem_raw[];
@@ -275,7 +275,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           break;
         }
         tc_fence_after();
-        const CUtensorMap* omap = h == 0 ? &amap : &bmap;
+        const CUtensorMap* omaps = h == 0 ? smaps.a : smaps.b;
         // the previous store from this warp's staging buffer must have read it
         if (lane == 0) bulk_wait_read0();
         __syncwarp();
@@ -305,7 +305,12 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
           const int p0 = phalf * 64;
           const int u = u0 + p0 / tl.vt, v = v0 + p0 % tl.vt;
           if (lane == 0 && u < tl.R && v < tl.S) {
-            tma_store_4d(omap, stage, v, u, quarter * 32, b);
+            // this warp's 32 channels; a destination map holds smaps.lq channels (one
+            // map unless the channels are scattered to their owner ranks)
+            for (int s2 = 0; s2 < 32; s2 += smaps.box_c) {
+              const int c = quarter * 32 + s2, q = c / smaps.lq;
+              tma_store_4d(omaps + q, stage + s2 * 128, v, u, c - q * smaps.lq, smaps.blk_base + b);
+            }
             bulk_commit();
           }
         }
@@ -316,6 +321,7 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       __syncwarp();
     }
     if (lane == 0) bulk_wait0();  // stores complete before the kernel ends
+    if (smaps.sys_fence) __threadfence_system();   // peers' planes: visible to their owners
   }
 
   tc_fence_before();
@@ -331,17 +337,16 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
 size_t input_stage_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
-                               const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
-                               const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
-                               float2* zstats, const PosTiling& tl, int incoming, int z_bf16,
-                               float eps, int* err, int grid, cudaStream_t stream, int test_stall) {
+                               const StoreMaps& smaps, const float* mask,
+                               const float* u_in, const float* v_in, float2* zstats,
+                               const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
+                               int grid, cudaStream_t stream, int test_stall) {
   cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, amap, bmap, mask, u_in,
-                                                               v_in, a_cm, b_cm, zstats, tl,
-                                                               incoming, z_bf16, eps, err,
-                                                               test_stall);
+  input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, smaps, mask, u_in,
+                                                               v_in, zstats, tl, incoming, z_bf16,
+                                                               eps, err, test_stall);
   return cudaGetLastError();
 }
 

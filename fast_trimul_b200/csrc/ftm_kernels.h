@@ -42,21 +42,41 @@ size_t input_stage_smem_bytes();
 size_t output_stage_smem_bytes();
 size_t contraction_smem_bytes();
 
+// Destinations of the input stage's a / b stores: one tensor map per destination
+// rank (one map, the local planes, when not sharded). Channel c of a tile goes to map
+// c / lq at channel coordinate c % lq and outer coordinate blk_base + batch index.
+constexpr int kMaxRanks = 8;
+struct StoreMaps {
+  CUtensorMap a[kMaxRanks];
+  CUtensorMap b[kMaxRanks];
+  int lq;          // channels per destination map
+  int box_c;       // channels per TMA store (min(32, lq))
+  int blk_base;    // outer coordinate offset (source rank * batch when scattering)
+  int sys_fence;   // peers read the stores: fence at system scope before exiting
+};
+
 cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
-                               const CUtensorMap& amap, const CUtensorMap& bmap, const float* mask,
-                               const float* u_in, const float* v_in, __half* a_cm, __half* b_cm,
-                               float2* zstats, const PosTiling& tl, int incoming, int z_bf16,
-                               float eps, int* err, int grid, cudaStream_t stream,
-                               int test_stall = 0);
+                               const StoreMaps& smaps, const float* mask,
+                               const float* u_in, const float* v_in, float2* zstats,
+                               const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
+                               int grid, cudaStream_t stream, int test_stall = 0);
 
 cudaError_t launch_contraction(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X, int L,
                                int M, int N, int K, int rows_per_block, int* err, int grid,
                                cudaStream_t stream);
 
+// Scattered X rows: row block xb (its owner) starts at base[xb]; channel l of this
+// launch is channel chan_off + l % lq of batch l / lq in the owner's (batch, c_total,
+// rows, n) plane.
+struct XDest {
+  __half* base[kMaxRanks];
+  int enabled, lq, c_total, chan_off;
+};
+
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
                                     int L, int M, int N, int K, int rows_per_block,
-                                    int a_rows_per_block, int* err,
-                                    int num_sms, cudaStream_t stream);
+                                    int a_rows_per_block, int* err, int num_sms,
+                                    cudaStream_t stream, const XDest* xdest = nullptr);
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
                                 const CUtensorMap& wmap, const CUtensorMap& omap,

@@ -75,6 +75,23 @@ class NativeStageOps:
                                              out.data_ptr(),
                                              self.err.data_ptr(), self._s()), "ftm_output_stage")
 
+    def input_stage_scatter(self, prob, z, mask, a_planes, b_planes, world, rank, group):
+        """Input stage writing each channel group straight into its owner's receive
+        plane (peer TMA stores; a_planes / b_planes: _lib.PeerPlanes)."""
+        import ctypes
+        _lib.check(self.lib.ftm_input_stage_scatter(
+            prob, z.data_ptr(), None if mask is None else mask.data_ptr(), self.packed.data_ptr(),
+            ctypes.byref(a_planes), ctypes.byref(b_planes), self._stats(z), self.err.data_ptr(),
+            self._s()), "ftm_input_stage_scatter")
+
+    def contraction_scatter(self, ar, br, x_planes, xr, batch, rows, n, world, rank, group):
+        """Contraction of this rank's channel shard with every x row stored straight
+        into its owner's x plane."""
+        import ctypes
+        _lib.check(self.lib.ftm_contraction_scatter(ar.data_ptr(), br.data_ptr(), ctypes.byref(x_planes),
+                                                    batch, C, rows, n, self.err.data_ptr(), self._s()),
+                   "ftm_contraction_scatter")
+
     def check(self):
         import ctypes
         d = ctypes.c_int(0)
@@ -125,11 +142,40 @@ class TorchStageOps:
             o = o * mask[..., None]
         out.copy_(o.to(out.dtype))
 
+    def input_stage_scatter(self, prob, z, mask, ar, br, world, rank, group):
+        """Same receive layout as the native scatter -- [source rank][batch][C/P][rows][n]
+        -- produced with an all-to-all instead of peer stores."""
+        B, rows, n = z.shape[0], z.shape[1], z.shape[2]
+        lq = C // world
+        a = torch.empty(B * C * rows * n, dtype=ar.dtype, device=ar.device)
+        b = torch.empty_like(a)
+        self.input_stage(prob, z, mask, a, b)
+        for src, dst in ((a, ar), (b, br)):
+            send = src.view(B, world, lq, rows, n).permute(1, 0, 2, 3, 4).contiguous().view(-1)
+            if world > 1:
+                dist.all_to_all_single(dst, send, group=group)
+            else:
+                dst.copy_(send)
+
+    def contraction_scatter(self, ar, br, x_planes, xr, batch, rows, n, world, rank, group):
+        """X rows of this rank's channels returned to their owners' channel-major planes."""
+        lq = C // world
+        L = batch * lq
+        xb = torch.empty(world * L * rows * n, dtype=xr.dtype, device=xr.device)
+        self.contraction(ar, br, xb, L, rows, n, world, a_blocks=world)   # [owner][L][rows][n]
+        recv = torch.empty_like(xb)                                        # [src][L][rows][n]
+        if world > 1:
+            dist.all_to_all_single(recv, xb, group=group)
+        else:
+            recv.copy_(xb)
+        xr.view(batch, world, lq, rows, n).copy_(
+            recv.view(world, batch, lq, rows, n).permute(1, 0, 2, 3, 4))
+
     def check(self):
         pass
 
 
-SCHEMES = ("allgather", "alltoall", "allgather_ce", "alltoall_ce")
+SCHEMES = ("allgather", "alltoall", "allgather_ce", "alltoall_ce", "fused")
 
 
 def default_scheme(world):
@@ -216,6 +262,10 @@ class RowShardedTriMul:
         if scheme not in SCHEMES:
             raise ValueError(f"scheme must be one of {SCHEMES}")
         self.scheme = scheme
+        if scheme == "fused":
+            chunks = 1
+            if C % self.world or (C // self.world) % 16:
+                raise ValueError("the fused exchange needs 128 / P channels per rank, a multiple of 16")
         if L % (chunks * (self.world if scheme.startswith("alltoall") else 1)):
             raise ValueError("channel chunks (x ranks for alltoall) must divide batch * 128")
         self.L, self.chunks, self.lc = L, chunks, L // chunks
@@ -243,6 +293,27 @@ class RowShardedTriMul:
             # gathered b, chunk-major: [chunk][rank][lc][rows][n]
             self.bg = torch.empty(chunks * self.world * self.lc * self.rows * n,
                                   dtype=torch.float16, device=dev)
+        elif scheme == "fused":
+            # receive planes written by the peers' kernels: a, b as
+            # [source rank][batch][C/P][rows][n]; x as this rank's channel-major plane
+            native_ops = isinstance(self.ops, NativeStageOps)
+            if native_ops:
+                self.win_a = PeerWindow(plane * 2, dev, group)
+                self.win_b = PeerWindow(plane * 2, dev, group)
+                self.win_x = PeerWindow(plane * 2, dev, group)
+                self.ar = self.win_a.tensor.view(torch.float16)
+                self.br = self.win_b.tensor.view(torch.float16)
+                self.xr = self.win_x.tensor.view(torch.float16)
+                P, r = self.world, self.rank
+                self.a_planes = _lib.PeerPlanes.make(P, r, self.win_a.ptrs)
+                self.b_planes = _lib.PeerPlanes.make(P, r, self.win_b.ptrs)
+                self.x_planes = _lib.PeerPlanes.make(P, r, self.win_x.ptrs)
+                self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+            else:
+                self.ar = torch.empty(plane, dtype=torch.float16, device=dev)
+                self.br = torch.empty(plane, dtype=torch.float16, device=dev)
+                self.xr = torch.empty(plane, dtype=torch.float16, device=dev)
+                self.a_planes = self.b_planes = self.x_planes = None
         elif scheme == "alltoall_ce":
             # receive windows written by the peers' copy engines (CUDA IPC mappings)
             self.win_a = PeerWindow(plane * 2, dev, group)
@@ -274,6 +345,8 @@ class RowShardedTriMul:
         if out is None:
             out = torch.empty(z_local.shape, dtype=self.out_dtype, device=z_local.device)
         ev = events
+        if self.scheme == "fused":
+            return self._forward_fused(z_local, mask_local, out, ev)
         if ev is not None:
             ev[0].record()
         self.ops.input_stage(self.prob, z_local, mask_local, self.a, self.b)
@@ -296,6 +369,39 @@ class RowShardedTriMul:
         if isinstance(self.ops, NativeStageOps):
             _lib.stats["calls"] += 1
             _lib.stats["kernel_launches"] += 2 + self.chunks
+        return out
+
+    def _forward_fused(self, z_local, mask_local, out, ev):
+        """Exchange fused into the kernels: the input stage stores each channel group of
+        a and b into its owner's receive plane, the contraction stores each x row into
+        its row owner's plane, and a device-side barrier separates the phases (a rank
+        reads a plane only after every writer's kernel has finished). The barrier after
+        the contraction also frees the a / b planes for the next call's input stage,
+        and x planes are rewritten only after their owner's next input stage, which
+        follows its output stage on the same stream."""
+        P, r = self.world, self.rank
+        native = isinstance(self.ops, NativeStageOps)
+        if ev is not None:
+            ev[0].record()
+        self.ops.input_stage_scatter(self.prob, z_local, mask_local,
+                                     self.a_planes if native else self.ar,
+                                     self.b_planes if native else self.br, P, r, self.group)
+        if native and P > 1:
+            dist.all_reduce(self.flag, group=self.group)
+        if ev is not None:
+            ev[1].record()
+        self.ops.contraction_scatter(self.ar, self.br, self.x_planes, self.xr, self.batch,
+                                     self.rows, self.n, P, r, self.group)
+        if native and P > 1:
+            dist.all_reduce(self.flag, group=self.group)
+        if ev is not None:
+            ev[2].record()
+        self.ops.output_stage(self.prob, z_local, mask_local, self.xr, out)
+        if ev is not None:
+            ev[3].record()
+        if native:
+            _lib.stats["calls"] += 1
+            _lib.stats["kernel_launches"] += 3
         return out
 
     def _exchange_allgather(self):

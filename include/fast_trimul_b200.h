@@ -126,6 +126,42 @@ int ftm_output_stage(const ftm_problem* p, const void* z, const float* mask, con
                      const float* zstats, const void* packed, void* out, int* err_word,
                      ftm_stream_t stream);
 
+/* ---- row-sharded multi-GPU forward, exchange fused into the kernels ----------
+ * No single counterpart in the reference (it has no multi-GPU path); this replaces
+ * the all-to-all that moves the projections a, b from row shards to channel shards
+ * and x back (the exchange around outgoing(), _kernels.py:131-146). With P ranks each
+ * owning `rows` consecutive rows of z, rank q owns channels [q*c_h/P, (q+1)*c_h/P).
+ * `base[q]` is rank q's receive plane as addressable from THIS GPU (a CUDA IPC or
+ * peer mapping; base[rank] is local). The kernels write into the peers' planes over
+ * NVLink themselves (TMA stores / stores from the epilogues); the caller orders the
+ * phases with a barrier across ranks (all writes into a plane complete -- every
+ * rank's kernel finished -- before its owner reads it). */
+#define FTM_MAX_RANKS 8
+typedef struct ftm_peer_planes {
+  int32_t world;                   /* P, 1..FTM_MAX_RANKS, c_h % P == 0 */
+  int32_t rank;                    /* this rank */
+  void* base[FTM_MAX_RANKS];       /* receive plane of rank q (16-byte aligned) */
+} ftm_peer_planes;
+
+/* Input stage (as ftm_input_stage, outgoing mode, p->rows = this rank's rows) whose
+ * a and b go straight to the channel owners: channel c of this rank's row i lands in
+ * rank q = c / (c_h/P) at  base[q] + (((rank*B + b)*(c_h/P) + c%(c_h/P))*rows + i)*cols + j
+ * (fp16 elements) -- the receive layout [source rank][batch][c_h/P][rows][cols].
+ * zstats stay local. Requires (c_h/P) % 16 == 0. */
+int ftm_input_stage_scatter(const ftm_problem* p, const void* z, const float* mask,
+                            const void* packed, const ftm_peer_planes* a_dst,
+                            const ftm_peer_planes* b_dst, float* zstats, int* err_word,
+                            ftm_stream_t stream);
+
+/* Contraction of this rank's channel shard over all P*rows rows, A and B in the
+ * receive layout above, with every x row written straight to its row owner:
+ * x[b][c][i][j] for c in this rank's channels, row i of owner o = i / rows, lands at
+ * base[o] + ((b*c_h + c)*rows + i%rows)*n + j -- the owner's local channel-major x
+ * plane (batch, c_h, rows, n), ready for ftm_output_stage. n = P * rows; rows % 256 == 0. */
+int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes* x_dst,
+                            int32_t batch, int32_t c_h, int32_t rows, int32_t n, int* err_word,
+                            ftm_stream_t stream);
+
 /* ---- whole forward with no allocation ---------------------------------------
  * No counterpart in the reference. For callers that cannot provide a workspace --
  * hosts with a fixed device-memory budget handed out at start-up, or hosts that may

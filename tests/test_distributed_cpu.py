@@ -46,7 +46,8 @@ def _worker(rank, world, port, n, chunks, result_path, scheme):
 
 
 @pytest.mark.parametrize("world,chunks,scheme", [(2, 4, "allgather"), (2, 1, "allgather"),
-                                                 (2, 4, "alltoall"), (4, 2, "alltoall")])
+                                                 (2, 4, "alltoall"), (4, 2, "alltoall"),
+                                                 (2, 1, "fused"), (4, 1, "fused")])
 def test_row_sharded_matches_oracle(tmp_path, world, chunks, scheme):
     from tests.helpers import compare, make_layer, oracle_out
     n = 16

@@ -51,7 +51,7 @@ def _worker(rank, world, port, path, scheme):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("scheme", ["allgather", "alltoall", "allgather_ce", "alltoall_ce"])
+@pytest.mark.parametrize("scheme", ["allgather", "alltoall", "allgather_ce", "alltoall_ce", "fused"])
 def test_two_gpu_row_sharding(tmp_path, scheme):
     from tests.helpers import MAX_ABS, MEAN_REL, compare, make_layer, oracle_out
     path = str(tmp_path / "o.npy")

@@ -62,7 +62,10 @@ SIGNATURES = {
                                                _vp, _vp]),
     "ftm_output_stage": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ftm_input_stage_scatter": (ctypes.c_int, [_PP, _vp, _vp, _vp, _PPL, _PPL, _vp, _vp, _vp]),
-    "ftm_contraction_scatter": (ctypes.c_int, [_vp, _vp, _PPL, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "ftm_contraction_scatter": (ctypes.c_int, [_vp, _vp, _PPL, _i32, _i32, _i32, _i32, _i32, _vp,
+                                               _vp]),
+    "ftm_contraction_kblocked": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
+                                                _vp, _vp]),
     "ftm_check_error": (ctypes.c_int, [_vp, _IP, _vp]),
     "ftm_workspace_error_word": (_vp, [_PP, _vp]),
     "ftm_status_string": (ctypes.c_char_p, [ctypes.c_int]),

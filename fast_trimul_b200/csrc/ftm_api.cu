@@ -92,7 +92,6 @@ int check_problem(const ftm_problem* p) {
   if (p->batch < 1 || p->rows < 1 || p->cols < 1) return FTM_BAD_SHAPE;
   if (p->cols % 8 != 0) return FTM_BAD_SHAPE;  // TMA row strides must be 16-byte multiples
   if (p->mode != FTM_OUTGOING && p->mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
-  if (p->mode == FTM_INCOMING && p->rows != p->cols) return FTM_BAD_SHAPE;
   if (p->z_dtype != FTM_F16 && p->z_dtype != FTM_BF16) return FTM_BAD_DTYPE;
   if (p->out_dtype != FTM_F16 && p->out_dtype != FTM_BF16 && p->out_dtype != FTM_F32)
     return FTM_BAD_DTYPE;
@@ -144,10 +143,13 @@ int test_stall_requested() {
 int stage_in(const ftm_problem* p, const void* z, const float* mask, const void* packed,
              void* a_cm, void* b_cm, float* zstats, int* err, cudaStream_t stream, int dev,
              const ftm_peer_planes* a_dst = nullptr, const ftm_peer_planes* b_dst = nullptr) {
-  PosTiling tl;
-  tl.init(p->batch, p->rows, p->cols);
-  tl.pf = prefetch_distance("FTM_PREFETCH_IN", 1);
+  // incoming: tiles run over (u = z column i, v = z row k), so a and b come out as the
+  // transposed planes [c][i][k] the contraction reads K-major (k = z row)
   const bool incoming = p->mode == FTM_INCOMING;
+  PosTiling tl;
+  if (incoming) tl.init(p->batch, p->cols, p->rows);
+  else tl.init(p->batch, p->rows, p->cols);
+  tl.pf = prefetch_distance("FTM_PREFETCH_IN", 1);
   CUtensorMap zmap, wmap;
   if (!make_z_map(&zmap, p, z, incoming, tl)) return FTM_LAUNCH_FAILED;
   const PackedLayout L = PackedLayout::make(kC, kC);
@@ -160,7 +162,7 @@ int stage_in(const ftm_problem* p, const void* z, const float* mask, const void*
   }
   // channel-major outputs: stores of [box_c channel x 64 position] blocks
   StoreMaps sm{};
-  const uint64_t R = p->rows, S = p->cols, B = p->batch;
+  const uint64_t R = tl.R, S = tl.S, B = p->batch;   // planes (B, C, R, S), S innermost
   if (!a_dst) {
     sm.lq = kC;
     sm.box_c = 32;
@@ -241,6 +243,35 @@ int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int 
     const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
     e = launch_contraction(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err, grid, stream);
   }
+  return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
+}
+
+// Contraction whose reduction index is split into k_blocks blocks of k_rpb (A, B stored
+// [k block][L][m or n][k_rpb] -- the channel-shard layout of the incoming transposed
+// planes), X written as (m / x_rpb) blocks of (L, x_rpb, n), or scattered to owners.
+int stage_contract_kblocked(const void* A, const void* B, void* X, int L, int m, int n, int k_rpb,
+                            int k_blocks, int x_rpb, int* err, cudaStream_t stream, int dev,
+                            const XDest* xdest = nullptr) {
+  CUtensorMap amap, bmap;
+  {
+    const uint64_t dims[4] = {uint64_t(k_rpb), uint64_t(m), uint64_t(L), uint64_t(k_blocks)};
+    const uint64_t strides[3] = {uint64_t(k_rpb) * 2, uint64_t(m) * k_rpb * 2,
+                                 uint64_t(L) * m * k_rpb * 2};
+    const uint32_t box[4] = {kCtBK, kCtBM, 1, 1};
+    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, A, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  {
+    const uint64_t dims[4] = {uint64_t(k_rpb), uint64_t(n), uint64_t(L), uint64_t(k_blocks)};
+    const uint64_t strides[3] = {uint64_t(k_rpb) * 2, uint64_t(n) * k_rpb * 2,
+                                 uint64_t(L) * n * k_rpb * 2};
+    const uint32_t box[4] = {kCtBK, 128u, 1, 1};
+    if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, B, dims, strides, box))
+      return FTM_LAUNCH_FAILED;
+  }
+  const cudaError_t e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n,
+                                                k_rpb * k_blocks, n, m, err, sm_count(dev), stream,
+                                                xdest, k_rpb, x_rpb);
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 
@@ -430,7 +461,6 @@ int ftm_input_stage_scatter(const ftm_problem* p, const void* z, const float* ma
   int st = check_problem(p);
   if (st != FTM_OK) return st;
   if (!z || !packed || !zstats || !err_word || !a_dst || !b_dst) return FTM_BAD_ARGUMENT;
-  if (p->mode != FTM_OUTGOING) return FTM_BAD_ARGUMENT;     // rows are sharded in outgoing mode
   if (!peers_ok(a_dst) || !peers_ok(b_dst) || a_dst->world != b_dst->world ||
       a_dst->rank != b_dst->rank)
     return FTM_BAD_ARGUMENT;
@@ -444,8 +474,8 @@ int ftm_input_stage_scatter(const ftm_problem* p, const void* z, const float* ma
 }
 
 int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes* x_dst,
-                            int32_t batch, int32_t c_h, int32_t rows, int32_t n, int* err_word,
-                            ftm_stream_t stream) {
+                            int32_t batch, int32_t c_h, int32_t rows, int32_t n, int32_t mode,
+                            int* err_word, ftm_stream_t stream) {
   g_last_launches = 0;
   if (!A || !B || !err_word || !x_dst) return FTM_BAD_ARGUMENT;
   if (c_h != kC || !peers_ok(x_dst)) return FTM_BAD_ARGUMENT;
@@ -460,9 +490,35 @@ int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes*
   xd.lq = lq;
   xd.c_total = kC;
   xd.chan_off = x_dst->rank * lq;
-  // A, B: P row blocks (one per source rank) of (batch * lq, rows, n)
-  const int st = stage_contract(A, B, x_dst->base[x_dst->rank], batch * lq, rows, P, n, rows, P,
-                                err_word, reinterpret_cast<cudaStream_t>(stream), dev, &xd);
+  // outgoing: A, B are P row blocks (one per source rank) of (batch * lq, rows, n);
+  // incoming: P blocks of the transposed planes (batch * lq, n, rows) -- k split by rank
+  if (mode != FTM_OUTGOING && mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
+  const int st =
+      mode == FTM_OUTGOING
+          ? stage_contract(A, B, x_dst->base[x_dst->rank], batch * lq, rows, P, n, rows, P, err_word,
+                           reinterpret_cast<cudaStream_t>(stream), dev, &xd)
+          : stage_contract_kblocked(A, B, x_dst->base[x_dst->rank], batch * lq, n, n, rows, P, rows,
+                                    err_word, reinterpret_cast<cudaStream_t>(stream), dev, &xd);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+int ftm_contraction_kblocked(const void* A, const void* B, void* X, int32_t L, int32_t m,
+                             int32_t n, int32_t k_rows_per_block, int32_t k_blocks,
+                             int32_t x_rows_per_block, int* err_word, ftm_stream_t stream) {
+  g_last_launches = 0;
+  if (!A || !B || !X || !err_word) return FTM_BAD_ARGUMENT;
+  if (L < 1 || m < 1 || n < 1 || k_rows_per_block < 1 || k_blocks < 1 || x_rows_per_block < 1)
+    return FTM_BAD_SHAPE;
+  if (k_rows_per_block % kCtBK != 0 || m % x_rows_per_block != 0 || n % 8 != 0 ||
+      (m / x_rows_per_block > 1 && x_rows_per_block % kCtBN != 0))
+    return FTM_BAD_SHAPE;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(X)) return FTM_BAD_ALIGN;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  const int st = stage_contract_kblocked(A, B, X, L, m, n, k_rows_per_block, k_blocks,
+                                         x_rows_per_block, err_word,
+                                         reinterpret_cast<cudaStream_t>(stream), dev);
   if (st == FTM_OK) g_last_launches = 1;
   return st;
 }

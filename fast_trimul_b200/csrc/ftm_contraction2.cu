@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
                         const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
                         int M, int N, int K, int rows_per_block, int a_rows_per_block,
-                        int* err, const XDest xd) {
+                        int k_rows_per_block, int x_rows_per_block, int* err, const XDest xd) {
   using Cfg = PairCfg<NH>;
   constexpr int kStages = Cfg::kStages, kStageBytes = Cfg::kStageBytes, kAcc = Cfg::kAcc;
   constexpr int kAccCols = Cfg::kAccCols;
@@ -169,10 +169,11 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
         const int i0 = tm * 2 * kBM + static_cast<int>(rank) * kBM;
         const int ablk = i0 / a_rows_per_block, ail = i0 - ablk * a_rows_per_block;
-        int bblk[NH], bjl[NH];
+        int bblk[NH], bjl[NH], bj0[NH];
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
           const int j0 = (tn * NH + h) * 2 * kBN + static_cast<int>(rank) * kBN;
+          bj0[h] = j0;
           bblk[h] = j0 / rows_per_block;
           bjl[h] = j0 - bblk[h] * rows_per_block;
         }
@@ -184,10 +185,18 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
           uint8_t* sa = smem + st * kStageBytes;
           const uint32_t fb = cluster_addr(&full[st], 0);
           if (leader) mbar_arrive_expect_tx(&full[st], 2 * kStageBytes);
-          tma_load_4d_pair(&amap, fb, sa, kb * kBK, ail, l, ablk);
+          // k split into blocks (one per source rank: A and B are [k block][l][row][k
+          // in block]) or contiguous; rows of A / B split into row blocks otherwise
+          const int kg = kb * kBK;
+          const int kblk = k_rows_per_block ? kg / k_rows_per_block : 0;
+          const int kc = k_rows_per_block ? kg - kblk * k_rows_per_block : kg;
+          tma_load_4d_pair(&amap, fb, sa, kc, k_rows_per_block ? i0 : ail, l,
+                           k_rows_per_block ? kblk : ablk);
 #pragma unroll
           for (int h = 0; h < NH; ++h)
-            tma_load_4d_pair(&bmap, fb, sa + kATile + h * kBTile, kb * kBK, bjl[h], l, bblk[h]);
+            tma_load_4d_pair(&bmap, fb, sa + kATile + h * kBTile, kc,
+                             k_rows_per_block ? bj0[h] : bjl[h], l,
+                             k_rows_per_block ? kblk : bblk[h]);
           ++issued;
           if (++st == kStages) {
             st = 0;
@@ -266,12 +275,12 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
       const int i = tm * 2 * kBM + static_cast<int>(rank) * kBM + sub * 32 + lane;
       // X rows are stored in blocks of a_rows_per_block like A: [block][l][row][col],
       // or -- scattered -- each block straight into its owner's channel-major plane
-      const int xb = i / a_rows_per_block, xi = i - xb * a_rows_per_block;
+      const int xb = i / x_rows_per_block, xi = i - xb * x_rows_per_block;
       __half* xrow =
           xd.enabled
               ? xd.base[xb] + ((static_cast<size_t>(l / xd.lq) * xd.c_total + xd.chan_off + l % xd.lq) *
-                                   a_rows_per_block + xi) * N
-              : X + ((static_cast<size_t>(xb) * L + l) * a_rows_per_block + xi) * N;
+                                   x_rows_per_block + xi) * N
+              : X + ((static_cast<size_t>(xb) * L + l) * x_rows_per_block + xi) * N;
       // 16-column chunks, the TMEM load of chunk ch + 1 in flight while chunk ch is
       // converted and stored
       uint32_t va[2][16];
@@ -328,7 +337,9 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
                                     int L, int M, int N, int K, int rows_per_block,
                                     int a_rows_per_block, int* err,
-                                    int num_sms, cudaStream_t stream, const XDest* xdest) {
+                                    int num_sms, cudaStream_t stream, const XDest* xdest,
+                                    int k_rows_per_block, int x_rows_per_block) {
+  if (x_rows_per_block <= 0) x_rows_per_block = a_rows_per_block;
   XDest xd{};
   if (xdest) xd = *xdest;
   // FTM_CT_NH=2 selects the 256 x 512 tile variant
@@ -352,7 +363,7 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, amap, bmap, X, L, M, N, K, rows_per_block,
-                           a_rows_per_block, err, xd);
+                           a_rows_per_block, k_rows_per_block, x_rows_per_block, err, xd);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };

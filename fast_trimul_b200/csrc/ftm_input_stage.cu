@@ -188,7 +188,8 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
       const bool valid = (u < tl.R) && (v < tl.S);
       // the mask load is issued before the wait so its latency hides behind the TMA
       // position of this row in z's natural (b, r, s) order
-      const size_t zi = incoming ? (static_cast<size_t>(b) * tl.R + v) * tl.S + u
+      // (incoming: the tiling runs over u = z column, v = z row, so z is (tl.S x tl.R))
+      const size_t zi = incoming ? (static_cast<size_t>(b) * tl.S + v) * tl.R + u
                                  : (static_cast<size_t>(b) * tl.R + u) * tl.S + v;
       float m = 0.f;
       if (valid) m = mask ? __ldg(mask + zi) : 1.f;

@@ -76,7 +76,8 @@ struct XDest {
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
                                     int L, int M, int N, int K, int rows_per_block,
                                     int a_rows_per_block, int* err, int num_sms,
-                                    cudaStream_t stream, const XDest* xdest = nullptr);
+                                    cudaStream_t stream, const XDest* xdest = nullptr,
+                                    int k_rows_per_block = 0, int x_rows_per_block = 0);
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
                                 const CUtensorMap& wmap, const CUtensorMap& omap,

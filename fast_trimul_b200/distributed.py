@@ -14,7 +14,10 @@ so with rank r owning z rows I_r (N/P of them):
 
 The reference has no multi-GPU path; this follows the row-sharding scheme the
 benchmark's multi-GPU configuration names (B=1, N=2048, outgoing). Incoming mode
-needs a column exchange instead and is not sharded here.
+(x[c,i,j] = sum_k a[c,k,i] b[c,k,j], k = z row) shards the same way through the
+channel-sharded schemes: each rank's input stage writes the transposed planes of its own
+rows k, the all-to-all hands every rank its channels with k split by source rank, and
+the contraction reduces over those k blocks (`ftm_contraction_kblocked`).
 
 `StageOps` isolates the three compute steps so the host-side logic (partitioning,
 buffer layout, chunked exchange) runs with torch stand-ins on CPU / gloo in tests.
@@ -63,6 +66,12 @@ class NativeStageOps:
                                             self._stats(z), self.err.data_ptr(), self._s()),
                    "ftm_input_stage")
 
+    def contraction_kblocked(self, a, b, x, L, n, rows, blocks):
+        """x (blocked by row owner) of incoming mode: k split into `blocks` source blocks."""
+        _lib.check(self.lib.ftm_contraction_kblocked(a.data_ptr(), b.data_ptr(), x.data_ptr(), L, n, n,
+                                                     rows, blocks, rows, self.err.data_ptr(), self._s()),
+                   "ftm_contraction_kblocked")
+
     def contraction(self, a, bblk, x, L, rows, n, blocks, a_blocks=1):
         _lib.check(self.lib.ftm_contraction_blocked(a.data_ptr(), bblk.data_ptr(), x.data_ptr(), L,
                                                     rows, a_blocks, n, rows, blocks,
@@ -84,12 +93,15 @@ class NativeStageOps:
             ctypes.byref(a_planes), ctypes.byref(b_planes), self._stats(z), self.err.data_ptr(),
             self._s()), "ftm_input_stage_scatter")
 
-    def contraction_scatter(self, ar, br, x_planes, xr, batch, rows, n, world, rank, group):
+    def contraction_scatter(self, ar, br, x_planes, xr, batch, rows, n, world, rank, group,
+                            mode="outgoing"):
         """Contraction of this rank's channel shard with every x row stored straight
         into its owner's x plane."""
         import ctypes
         _lib.check(self.lib.ftm_contraction_scatter(ar.data_ptr(), br.data_ptr(), ctypes.byref(x_planes),
-                                                    batch, C, rows, n, self.err.data_ptr(), self._s()),
+                                                    batch, C, rows, n,
+                                                    _lib.OUTGOING if mode == "outgoing" else _lib.INCOMING,
+                                                    self.err.data_ptr(), self._s()),
                    "ftm_contraction_scatter")
 
     def check(self):
@@ -115,12 +127,21 @@ class TorchStageOps:
         return zz, zn, p
 
     def input_stage(self, prob, z, mask, a, b):
+        """Channel planes [b][c][i][j]; incoming mode writes them transposed, [b][c][i][k]
+        with k the z row, as the native input stage does."""
         import torch.nn.functional as F
         _, zn, p = self._proj(z, mask)
         av = F.linear(zn, p[4], p[5]) * torch.sigmoid(F.linear(zn, p[6], p[7]))
         bv = F.linear(zn, p[8], p[9]) * torch.sigmoid(F.linear(zn, p[10], p[11]))
-        a.copy_(av.permute(0, 3, 1, 2).reshape(-1).to(a.dtype))
-        b.copy_(bv.permute(0, 3, 1, 2).reshape(-1).to(b.dtype))
+        perm = (0, 3, 1, 2) if self.impl.mode == "outgoing" else (0, 3, 2, 1)
+        a.copy_(av.permute(*perm).reshape(-1).to(a.dtype))
+        b.copy_(bv.permute(*perm).reshape(-1).to(b.dtype))
+
+    def contraction_kblocked(self, a, b, x, L, n, rows, blocks):
+        def unblock(t):      # [k block][L][n][rows] -> (L, n, blocks * rows)
+            return t.view(blocks, L, n, rows).permute(1, 2, 0, 3).reshape(L, n, blocks * rows).float()
+        X = torch.bmm(unblock(a), unblock(b).transpose(1, 2))               # (L, n, n)
+        x.view(n // rows, L, rows, n).copy_(X.view(L, n // rows, rows, n).permute(1, 0, 2, 3).to(x.dtype))
 
     def contraction(self, a, bblk, x, L, rows, n, blocks, a_blocks=1):
         def unblock(t, nb):
@@ -157,12 +178,16 @@ class TorchStageOps:
             else:
                 dst.copy_(send)
 
-    def contraction_scatter(self, ar, br, x_planes, xr, batch, rows, n, world, rank, group):
+    def contraction_scatter(self, ar, br, x_planes, xr, batch, rows, n, world, rank, group,
+                            mode="outgoing"):
         """X rows of this rank's channels returned to their owners' channel-major planes."""
         lq = C // world
         L = batch * lq
         xb = torch.empty(world * L * rows * n, dtype=xr.dtype, device=xr.device)
-        self.contraction(ar, br, xb, L, rows, n, world, a_blocks=world)   # [owner][L][rows][n]
+        if mode == "outgoing":
+            self.contraction(ar, br, xb, L, rows, n, world, a_blocks=world)   # [owner][L][rows][n]
+        else:
+            self.contraction_kblocked(ar, br, xb, L, n, rows, world)
         recv = torch.empty_like(xb)                                        # [src][L][rows][n]
         if world > 1:
             dist.all_to_all_single(recv, xb, group=group)
@@ -178,11 +203,11 @@ class TorchStageOps:
 SCHEMES = ("allgather", "alltoall", "allgather_ce", "alltoall_ce", "fused")
 
 
-def default_scheme(world):
+def default_scheme(world, mode="outgoing"):
     """Copy-engine exchanges; all-gather of b moves fewer bytes at 2 ranks, the
     channel-sharded all-to-all from 4 ranks on (measured N=2048: 2 GPUs 1408 vs
-    1228 TFLOP/s, 4 GPUs 1961 vs 1662)."""
-    return "allgather_ce" if world <= 2 else "alltoall_ce"
+    1228 TFLOP/s, 4 GPUs 1961 vs 1662). Incoming mode always shards by channel."""
+    return "allgather_ce" if world <= 2 and mode == "outgoing" else "alltoall_ce"
 
 
 class PeerWindow:
@@ -246,8 +271,10 @@ class RowShardedTriMul:
 
     def __init__(self, impl, batch, n, group=None, z_dtype=torch.bfloat16, out_dtype=None,
                  chunks=4, device=None, ops=None, scheme="allgather"):
-        if impl.mode != "outgoing":
-            raise NotImplementedError("row sharding covers outgoing mode")
+        self.mode = impl.mode
+        if impl.mode != "outgoing" and scheme not in ("alltoall", "alltoall_ce", "fused"):
+            raise NotImplementedError("incoming mode is sharded by the channel-sharded schemes "
+                                      "(alltoall, alltoall_ce, fused)")
         self.impl, self.group = impl, group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -391,7 +418,7 @@ class RowShardedTriMul:
         if ev is not None:
             ev[1].record()
         self.ops.contraction_scatter(self.ar, self.br, self.x_planes, self.xr, self.batch,
-                                     self.rows, self.n, P, r, self.group)
+                                     self.rows, self.n, P, r, self.group, mode=self.mode)
         if native and P > 1:
             dist.all_reduce(self.flag, group=self.group)
         if ev is not None:
@@ -403,6 +430,15 @@ class RowShardedTriMul:
             _lib.stats["calls"] += 1
             _lib.stats["kernel_launches"] += 3
         return out
+
+    def _contract_shard(self, A, B, X, L):
+        """This rank's channels over all rows, X blocked by row owner: outgoing reads row
+        blocks of A and B; incoming reads the transposed planes with k split by source."""
+        P = self.world
+        if self.mode == "outgoing":
+            self.ops.contraction(A, B, X, L, self.rows, self.n, P, a_blocks=P)
+        else:
+            self.ops.contraction_kblocked(A, B, X, L, self.n, self.rows, P)
 
     def _exchange_allgather(self):
         """All-gather b chunk by chunk; contract each chunk as soon as it lands."""
@@ -442,8 +478,7 @@ class RowShardedTriMul:
             ins[k][0].wait()
             ins[k][1].wait()
             # A and B: P row blocks (one per source rank) of lq channels; X blocked by row owner
-            self.ops.contraction(self.ar[sl], self.br[sl], self.xb[sl], lq, self.rows, self.n, P,
-                                 a_blocks=P)
+            self._contract_shard(self.ar[sl], self.br[sl], self.xb[sl], lq)
             outs.append(dist.all_to_all_single(self.xr[sl], self.xb[sl], group=self.group,
                                                async_op=True))
         for w in outs:
@@ -525,7 +560,7 @@ class RowShardedTriMul:
             comp.wait_event(done[k])
             elems = self.lc * rows * n
             sl = slice(k * elems, (k + 1) * elems)
-            self.ops.contraction(self.ar[sl], self.br[sl], self.xb[sl], lq, rows, n, P, a_blocks=P)
+            self._contract_shard(self.ar[sl], self.br[sl], self.xb[sl], lq)
             ev = torch.cuda.Event()
             ev.record(comp)
             # x rows of owner p (my channels) -> p's channel-major x at my channel block
@@ -555,12 +590,13 @@ def bench_sharded(args, torch_mod):
         dist.init_process_group("nccl", device_id=dev)
     n = args.n
     torch.manual_seed(0)
-    layer = FastTriangleMultiplication(C, C, mode="outgoing", residual=True).to(dev).eval()
+    mode = getattr(args, "mode", "outgoing") or "outgoing"
+    layer = FastTriangleMultiplication(C, C, mode=mode, residual=True).to(dev).eval()
     lo, hi = row_range(n, world, rank)
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     z = torch.randn(1, hi - lo, n, C, device=dev, generator=gen).to(torch.bfloat16)
     mask = torch.ones(1, hi - lo, n, device=dev)
-    scheme = getattr(args, "scheme", None) or default_scheme(world)
+    scheme = getattr(args, "scheme", None) or default_scheme(world, mode)
     chunks = getattr(args, "chunks", None) or (4 if scheme.startswith("allgather") else 2)
     sh = RowShardedTriMul(layer._impl, 1, n, chunks=chunks, device=dev, scheme=scheme)
     out = torch.empty_like(z)

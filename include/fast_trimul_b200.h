@@ -118,6 +118,18 @@ int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
                             int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
                             ftm_stream_t stream);
 
+/* Contraction with the reduction index split into blocks:
+ * X[l][i][j] = sum_k A[l][i][k] * B[l][j][k] with A stored as k_blocks blocks of
+ * (L, m, k_rows_per_block) and B as k_blocks blocks of (L, n, k_rows_per_block) --
+ * block q holding k in [q*k_rows_per_block, (q+1)*k_rows_per_block) -- and X written as
+ * m / x_rows_per_block blocks of (L, x_rows_per_block, n). This is incoming mode's
+ * contraction (_kernels.py:148-162) on channel shards gathered from row-sharded z
+ * (each rank's transposed planes carry its own rows k). Requires k_rows_per_block % 64 == 0
+ * and, when X has more than one block, x_rows_per_block % 256 == 0. */
+int ftm_contraction_kblocked(const void* A, const void* B, void* X, int32_t L, int32_t m,
+                             int32_t n, int32_t k_rows_per_block, int32_t k_blocks,
+                             int32_t x_rows_per_block, int* err_word, ftm_stream_t stream);
+
 /* Output stage: LayerNorm over c_h of x (channel-major fp16), the c_h -> c_z projection,
  * sigmoid(z_n W_g + b_g) gate, residual and mask, stored in out_dtype. Replaces
  * layer_norm + KernelLinear.raw x2 + gated_residual/gate + the mask/cast glue
@@ -143,24 +155,26 @@ typedef struct ftm_peer_planes {
   void* base[FTM_MAX_RANKS];       /* receive plane of rank q (16-byte aligned) */
 } ftm_peer_planes;
 
-/* Input stage (as ftm_input_stage, outgoing mode, p->rows = this rank's rows) whose
- * a and b go straight to the channel owners: channel c of this rank's row i lands in
- * rank q = c / (c_h/P) at  base[q] + (((rank*B + b)*(c_h/P) + c%(c_h/P))*rows + i)*cols + j
- * (fp16 elements) -- the receive layout [source rank][batch][c_h/P][rows][cols].
- * zstats stay local. Requires (c_h/P) % 16 == 0. */
+/* Input stage (as ftm_input_stage, p->rows = this rank's rows) whose a and b go
+ * straight to the channel owners: rank q = c / (c_h/P) receives this rank's planes of
+ * its channels at  base[q] + ((rank*B + b)*(c_h/P) + c%(c_h/P))*rows*cols  (fp16
+ * elements) -- the receive layout [source rank][batch][c_h/P][plane]. The plane is
+ * (rows, cols) [i][j] in outgoing mode and the transposed (cols, rows) [i][k] in incoming
+ * mode, as ftm_input_stage writes them. zstats stay local. Requires (c_h/P) % 16 == 0. */
 int ftm_input_stage_scatter(const ftm_problem* p, const void* z, const float* mask,
                             const void* packed, const ftm_peer_planes* a_dst,
                             const ftm_peer_planes* b_dst, float* zstats, int* err_word,
                             ftm_stream_t stream);
 
-/* Contraction of this rank's channel shard over all P*rows rows, A and B in the
- * receive layout above, with every x row written straight to its row owner:
+/* Contraction of this rank's channel shard over all n = P*rows rows (mode outgoing:
+ * A, B are the row blocks of the receive layout above; incoming: the transposed planes,
+ * so k is split by source rank), with every x row written straight to its row owner:
  * x[b][c][i][j] for c in this rank's channels, row i of owner o = i / rows, lands at
  * base[o] + ((b*c_h + c)*rows + i%rows)*n + j -- the owner's local channel-major x
- * plane (batch, c_h, rows, n), ready for ftm_output_stage. n = P * rows; rows % 256 == 0. */
+ * plane (batch, c_h, rows, n), ready for ftm_output_stage. rows % 256 == 0. */
 int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes* x_dst,
-                            int32_t batch, int32_t c_h, int32_t rows, int32_t n, int* err_word,
-                            ftm_stream_t stream);
+                            int32_t batch, int32_t c_h, int32_t rows, int32_t n, int32_t mode,
+                            int* err_word, ftm_stream_t stream);
 
 /* ---- whole forward with no allocation ---------------------------------------
  * No counterpart in the reference. For callers that cannot provide a workspace --

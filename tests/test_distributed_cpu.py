@@ -21,13 +21,13 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, n, chunks, result_path, scheme):
+def _worker(rank, world, port, n, chunks, result_path, scheme, mode="outgoing"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from fast_trimul_b200.distributed import RowShardedTriMul, TorchStageOps, row_range
         from tests.helpers import make_layer
-        m = make_layer("outgoing", True, d=128)
+        m = make_layer(mode, True, d=128)
         gen = torch.Generator().manual_seed(9)
         z = torch.randn(1, n, n, 128, generator=gen)
         mask = torch.ones(1, n, n)
@@ -45,17 +45,19 @@ def _worker(rank, world, port, n, chunks, result_path, scheme):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,chunks,scheme", [(2, 4, "allgather"), (2, 1, "allgather"),
-                                                 (2, 4, "alltoall"), (4, 2, "alltoall"),
-                                                 (2, 1, "fused"), (4, 1, "fused")])
-def test_row_sharded_matches_oracle(tmp_path, world, chunks, scheme):
+@pytest.mark.parametrize("world,chunks,scheme,mode", [
+    (2, 4, "allgather", "outgoing"), (2, 1, "allgather", "outgoing"),
+    (2, 4, "alltoall", "outgoing"), (4, 2, "alltoall", "outgoing"),
+    (2, 1, "fused", "outgoing"), (4, 1, "fused", "outgoing"),
+    (2, 2, "alltoall", "incoming"), (4, 1, "alltoall", "incoming"), (2, 1, "fused", "incoming")])
+def test_row_sharded_matches_oracle(tmp_path, world, chunks, scheme, mode):
     from tests.helpers import compare, make_layer, oracle_out
     n = 16
     path = str(tmp_path / "out.npy")
-    mp.start_processes(_worker, args=(world, _free_port(), n, chunks, path, scheme), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), n, chunks, path, scheme, mode),
+                       nprocs=world, join=True, start_method="spawn")
     got = torch.from_numpy(np.load(path))
-    m = make_layer("outgoing", True, d=128)
+    m = make_layer(mode, True, d=128)
     gen = torch.Generator().manual_seed(9)
     z = torch.randn(1, n, n, 128, generator=gen)
     mask = torch.ones(1, n, n)

@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, path, scheme):
+def _worker(rank, world, port, path, scheme, mode="outgoing"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -32,7 +32,7 @@ def _worker(rank, world, port, path, scheme):
     try:
         from fast_trimul_b200.distributed import RowShardedTriMul, row_range
         from tests.helpers import make_layer
-        m = make_layer("outgoing", True).to(dev)
+        m = make_layer(mode, True).to(dev)
         gen = torch.Generator().manual_seed(21)
         z = torch.randn(1, N, N, 128, generator=gen).to(torch.bfloat16)
         mask = torch.ones(1, N, N)
@@ -51,14 +51,17 @@ def _worker(rank, world, port, path, scheme):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("scheme", ["allgather", "alltoall", "allgather_ce", "alltoall_ce", "fused"])
-def test_two_gpu_row_sharding(tmp_path, scheme):
+@pytest.mark.parametrize("scheme,mode", [("allgather", "outgoing"), ("alltoall", "outgoing"),
+                                         ("allgather_ce", "outgoing"), ("alltoall_ce", "outgoing"),
+                                         ("fused", "outgoing"), ("alltoall_ce", "incoming"),
+                                         ("fused", "incoming")])
+def test_two_gpu_row_sharding(tmp_path, scheme, mode):
     from tests.helpers import MAX_ABS, MEAN_REL, compare, make_layer, oracle_out
     path = str(tmp_path / "o.npy")
-    mp.start_processes(_worker, args=(2, _free_port(), path, scheme), nprocs=2, join=True,
+    mp.start_processes(_worker, args=(2, _free_port(), path, scheme, mode), nprocs=2, join=True,
                        start_method="spawn")
     got = torch.from_numpy(np.load(path))
-    m = make_layer("outgoing", True)
+    m = make_layer(mode, True)
     gen = torch.Generator().manual_seed(21)
     z = torch.randn(1, N, N, 128, generator=gen).to(torch.bfloat16)
     mask = torch.ones(1, N, N)

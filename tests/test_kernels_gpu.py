@@ -183,6 +183,58 @@ def test_contraction_blocked_a_and_x():
 
 
 @needs_gpu
+@pytest.mark.parametrize("kernel", ["pair", "pair_wide"])
+def test_contraction_kblocked(kernel, monkeypatch):
+    """k split into source blocks (incoming mode's channel shards): A, B as
+    [k block][L][m][k_rpb], X blocked by row owner."""
+    _select_contraction(kernel, monkeypatch)
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    L, n, rows, blocks = 3, 512, 256, 2
+    g = torch.Generator(device="cuda").manual_seed(10)
+    Ab = torch.randn(blocks, L, n, rows, device="cuda", generator=g).half()
+    Bb = torch.randn(blocks, L, n, rows, device="cuda", generator=g).half()
+    X = torch.full((n // rows, L, rows, n), float("nan"), device="cuda", dtype=torch.half)
+    err = torch.zeros(64, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.ftm_contraction_kblocked(Ab.data_ptr(), Bb.data_ptr(), X.data_ptr(), L, n, n, rows,
+                                        blocks, rows, err.data_ptr(), s) == 0
+    assert lib.ftm_check_error(err.data_ptr(), None, s) == 0
+    A = Ab.permute(1, 2, 0, 3).reshape(L, n, blocks * rows).float()
+    B = Bb.permute(1, 2, 0, 3).reshape(L, n, blocks * rows).float()
+    ref = torch.bmm(A, B.transpose(1, 2)).view(L, n // rows, rows, n).permute(1, 0, 2, 3)
+    assert torch.isfinite(X).all()
+    rel = ((X.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 2e-3, rel
+
+
+@needs_gpu
+def test_input_stage_incoming_row_shard():
+    """Incoming mode on a non-square row shard (rows != cols): the transposed planes
+    [c][i][k] of this shard's rows k, against the torch stand-in of the same stage."""
+    from fast_trimul_b200 import _lib
+    from fast_trimul_b200.distributed import NativeStageOps, TorchStageOps
+    m = make_layer("incoming", True).cuda()
+    rows, n = 128, 384
+    g = torch.Generator(device="cuda").manual_seed(12)
+    z = torch.randn(1, rows, n, 128, device="cuda", generator=g).to(torch.bfloat16)
+    mask = torch.ones(1, rows, n, device="cuda")
+    mask[:, :, n - 20:] = 0
+    prob = m._impl.problem(z, torch.bfloat16)
+    plane = 128 * rows * n
+    a = torch.empty(plane, dtype=torch.float16, device="cuda")
+    b = torch.empty_like(a)
+    ops = NativeStageOps(m._impl, z.device)
+    ops.input_stage(prob, z, mask, a, b)
+    ops.check()
+    ra, rb = torch.empty(plane, dtype=torch.float32, device="cuda"), torch.empty(plane, device="cuda")
+    TorchStageOps(m._impl).input_stage(prob, z, mask, ra, rb)
+    for got, ref in ((a, ra), (b, rb)):
+        d = (got.float() - ref).abs()
+        assert d.max().item() < 2e-2 and d.mean().item() / ref.abs().mean().item() < 3e-3
+
+
+@needs_gpu
 def test_output_canaries_and_error_word():
     """Writes stay inside `out` (guard regions untouched) and no wait timed out."""
     from fast_trimul_b200 import _lib

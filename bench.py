@@ -244,11 +244,11 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------------------- ours, 1 GPU
-def make_layer(device):
+def make_layer(device, mode="outgoing"):
     import torch
     from fast_trimul_b200 import FastTriangleMultiplication
     torch.manual_seed(0)
-    return FastTriangleMultiplication(C, C, mode="outgoing", residual=True).to(device).eval()
+    return FastTriangleMultiplication(C, C, mode=mode, residual=True).to(device).eval()
 
 
 def bench_single(args, torch):
@@ -256,7 +256,7 @@ def bench_single(args, torch):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     n = args.n
-    layer = make_layer(dev)
+    layer = make_layer(dev, getattr(args, "mode", "outgoing"))
     gen = torch.Generator(device=dev).manual_seed(1)
     z = torch.randn(1, n, n, C, device=dev, generator=gen).to(torch.bfloat16)
     mask = torch.ones(1, n, n, device=dev)
@@ -392,6 +392,7 @@ def bench_sweep(args, torch, layer, dev):
     """Latency / TFLOP/s at the other sizes the metric names (median of per-step events)."""
     from fast_trimul_b200.plan import TriMulPlan
     rows = []
+    mode0 = layer._impl.mode
     for n, mode in ((256, "outgoing"), (256, "incoming"), (512, "outgoing"), (1024, "outgoing"),
                     (1024, "incoming"), (2048, "incoming")):
         layer._impl.mode = mode
@@ -414,7 +415,7 @@ def bench_sweep(args, torch, layer, dev):
         rows.append({"n": n, "mode": mode, "ms": round(ms, 4),
                      "tflops": round(trimul_flops(1, n) / (ms * 1e-3) / 1e12, 2)})
         del plan, z, out
-    layer._impl.mode = "outgoing"
+    layer._impl.mode = mode0
     return rows
 
 
@@ -536,7 +537,7 @@ def profile_case(args):
     n = args.profile_case
     if args.profile_shard:
         return profile_shard(args, torch, dev, n, args.profile_shard)
-    layer = make_layer(dev)
+    layer = make_layer(dev, getattr(args, "mode", "outgoing"))
     layer._impl.mode = args.mode
     z = torch.randn(1, n, n, C, device=dev).to(torch.bfloat16)
     mask = torch.ones(1, n, n, device=dev)
@@ -555,7 +556,7 @@ def profile_shard(args, torch, dev, n, P):
     from fast_trimul_b200 import _lib
     from fast_trimul_b200.distributed import RowShardedTriMul, TorchStageOps  # noqa: F401
     lib = _lib.load()
-    layer = make_layer(dev)
+    layer = make_layer(dev, getattr(args, "mode", "outgoing"))
     R = n // P
     z = torch.randn(1, R, n, C, device=dev).to(torch.bfloat16)
     mask = torch.ones(1, R, n, device=dev)
@@ -659,8 +660,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (z ~ N(0,1) bf16, ones mask, seeded random-init weights)",
-        "config": {"workload": f"C5 outgoing TriMul B=1 N={n} c_z=c_h=128", "batch": 1, "n": n,
-                   "c_z": C, "c_h": C, "mode": "outgoing", "z_dtype": "bf16",
+        "config": {"workload": f"C5 {args.mode} TriMul B=1 N={n} c_z=c_h=128", "batch": 1, "n": n,
+                   "c_z": C, "c_h": C, "mode": args.mode, "z_dtype": "bf16",
                    "parallelism": f"i-row shards x{max(world, args.gpus)}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (z = %.2f GB)" % (n * n * C * 2 / 1e9)},
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1),

@@ -250,34 +250,43 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
         m = mask ? __ldg(mask + zi) : 1.f;
         zst = __ldg(zstats + zi);
       }
-      if (!mbar_wait(&full_x[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
+      // warp-uniform: the statistics below exchange partial sums between lanes
+      if (!mbar_wait_warp(&full_x[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 1)))
         break;
       uint8_t* zs = sSlots + s * kSlot;
       const uint8_t* xs = zs + kZTile;
       const float inv_c = 1.0f / kC;
       float dm;
-      // x column statistics: element (c, row) of the MN-major x tile
-      const int h = row >> 6, e = row & 63;
+      // x column statistics of the MN-major x tile, two positions per thread pair:
+      // threads row and row ^ 1 own positions pr, pr + 1 and split the channels in
+      // halves; each reads half2 words (both positions of one channel), accumulates the
+      // two positions in the lanes of FADD2 / FFMA2, and the halves are then combined
+      // with the partner by shuffle. Channel 0 of each position is its shift.
+      const int pr = row & ~1, chh = row & 1;
+      const int h = pr >> 6, e = pr & 63;
       const uint8_t* xcol = xs + h * kHalfTile + (e & 7) * 2;
-      const float xshift = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(0, e >> 3)));
-      // channel pairs in packed fp32x2 (FADD2 / FFMA2): eight partial sums in four pairs
+      const float2 shift = __half22float2(*reinterpret_cast<const __half2*>(xcol + sw128_off(0, e >> 3)));
+      const float2 nshift = make_float2(-shift.x, -shift.y);
       float2 a1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       float2 a2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 nshift = make_float2(-xshift, -xshift);
 #pragma unroll 8
-      for (int c = 0; c < kC; c += 4) {
+      for (int c = chh * (kC / 2); c < chh * (kC / 2) + kC / 2; c += 2) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-          const float x0 = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c + 2 * k, e >> 3)));
-          const float x1 = __half2float(*reinterpret_cast<const __half*>(xcol + sw128_off(c + 2 * k + 1, e >> 3)));
-          const float2 d = __fadd2_rn(make_float2(x0, x1), nshift);
+          const float2 xv = __half22float2(*reinterpret_cast<const __half2*>(xcol + sw128_off(c + k, e >> 3)));
+          const float2 d = __fadd2_rn(xv, nshift);
           a1[k] = __fadd2_rn(a1[k], d);
           a2[k] = __ffma2_rn(d, d, a2[k]);
         }
       }
-      dm = ((a1[0].x + a1[0].y) + (a1[1].x + a1[1].y)) * inv_c;
-      const float mean_x = xshift + dm;
-      const float var_x = fmaxf(((a2[0].x + a2[0].y) + (a2[1].x + a2[1].y)) * inv_c - dm * dm, 0.f);
+      float2 s1 = __fadd2_rn(a1[0], a1[1]), s2 = __fadd2_rn(a2[0], a2[1]);
+      s1.x += __shfl_xor_sync(0xffffffffu, s1.x, 1);
+      s1.y += __shfl_xor_sync(0xffffffffu, s1.y, 1);
+      s2.x += __shfl_xor_sync(0xffffffffu, s2.x, 1);
+      s2.y += __shfl_xor_sync(0xffffffffu, s2.y, 1);
+      dm = (chh ? s1.y : s1.x) * inv_c;
+      const float mean_x = (chh ? shift.y : shift.x) + dm;
+      const float var_x = fmaxf((chh ? s2.y : s2.x) * inv_c - dm * dm, 0.f);
       if (!mbar_wait(&full_z[s], (it / kOutBufs) & 1, err, err_code(KERNEL_OUTPUT, ROLE_TRANSFORM, 2)))
         break;
       if (z_bf16) {   // bf16 -> fp16 in place (exact inside fp16 range): the MMA operand

@@ -105,4 +105,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FAST_TRIMUL_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference checkout> (or set FAST_TRIMUL_REFERENCE)")
+    main(ref)

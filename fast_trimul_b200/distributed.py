@@ -304,8 +304,9 @@ class RowShardedTriMul:
         probe = torch.empty(batch, self.rows, n, C, dtype=z_dtype, device="meta")
         self.prob = impl.problem(probe, self.out_dtype)
         plane = L * self.rows * n
-        self.a = torch.empty(plane, dtype=torch.float16, device=dev)
-        self.b = torch.empty(plane, dtype=torch.float16, device=dev)
+        if scheme != "fused":     # the fused scheme's input stage writes the peers' planes
+            self.a = torch.empty(plane, dtype=torch.float16, device=dev)
+            self.b = torch.empty(plane, dtype=torch.float16, device=dev)
         if scheme == "allgather_ce":
             self.x = torch.empty(plane, dtype=torch.float16, device=dev)
             # gathered b window, chunk-major [chunk][src rank][lc][rows][n], written by

@@ -362,6 +362,14 @@ class RowShardedTriMul:
             self.xb = torch.empty(plane, dtype=torch.float16, device=dev)
             self.xr = torch.empty(plane, dtype=torch.float16, device=dev)
 
+    def close(self):
+        """Unmap the peers' receive windows (CUDA IPC handles). Call on every rank after
+        the last forward, before the process group is destroyed."""
+        for name in ("win_a", "win_b", "win_x"):
+            w = getattr(self, name, None)
+            if w is not None:
+                w.close()
+
     def comm_bytes_per_step(self):
         """Bytes each rank receives over the interconnect per forward."""
         plane = self.L * self.rows * self.n * 2

@@ -92,6 +92,8 @@ int check_problem(const ftm_problem* p) {
   if (p->batch < 1 || p->rows < 1 || p->cols < 1) return FTM_BAD_SHAPE;
   if (p->cols % 8 != 0) return FTM_BAD_SHAPE;  // TMA row strides must be 16-byte multiples
   if (p->mode != FTM_OUTGOING && p->mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
+  // incoming mode writes the transposed planes (rows innermost): same 16-byte rule
+  if (p->mode == FTM_INCOMING && p->rows % 8 != 0) return FTM_BAD_SHAPE;
   if (p->z_dtype != FTM_F16 && p->z_dtype != FTM_BF16) return FTM_BAD_DTYPE;
   if (p->out_dtype != FTM_F16 && p->out_dtype != FTM_BF16 && p->out_dtype != FTM_F32)
     return FTM_BAD_DTYPE;
@@ -479,6 +481,7 @@ int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes*
   g_last_launches = 0;
   if (!A || !B || !err_word || !x_dst) return FTM_BAD_ARGUMENT;
   if (c_h != kC || !peers_ok(x_dst)) return FTM_BAD_ARGUMENT;
+  if (mode != FTM_OUTGOING && mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
   const int P = x_dst->world, lq = kC / P;
   if (batch < 1 || rows < 1 || n != P * rows || rows % kCtBN != 0) return FTM_BAD_SHAPE;
   if (!aligned16(A) || !aligned16(B)) return FTM_BAD_ALIGN;
@@ -492,7 +495,6 @@ int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes*
   xd.chan_off = x_dst->rank * lq;
   // outgoing: A, B are P row blocks (one per source rank) of (batch * lq, rows, n);
   // incoming: P blocks of the transposed planes (batch * lq, n, rows) -- k split by rank
-  if (mode != FTM_OUTGOING && mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
   const int st =
       mode == FTM_OUTGOING
           ? stage_contract(A, B, x_dst->base[x_dst->rank], batch * lq, rows, P, n, rows, P, err_word,

@@ -272,3 +272,46 @@ def test_clock_sampler_summary_reads_nvml_reason_bits():
     assert s["sm_mhz"] == 1930.0                       # idle sample (345) left out
     assert s["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
     assert ClockSampler(0).summary()["samples"] == 0
+
+
+def test_c_abi_rejects_bad_arguments_before_touching_a_device():
+    """Argument checks of the multi-GPU and blocked entry points run on the host and
+    return a status before any device call (here, without a GPU, valid arguments stop at
+    FTM_UNSUPPORTED_ARCH); nothing is launched."""
+    import ctypes
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    fake = ctypes.c_void_p(1 << 20)          # 16-byte aligned, never dereferenced
+    err = ctypes.c_void_p(1 << 20)
+
+    def prob(rows, cols, mode=_lib.OUTGOING):
+        return _lib.Problem(1, rows, cols, 128, 128, mode, 1, _lib.BF16, _lib.BF16, 1e-5, 1e-5)
+
+    planes = _lib.PeerPlanes.make(2, 0, [1 << 20, 2 << 20])
+    bad_world = _lib.PeerPlanes.make(3, 0, [1 << 20, 2 << 20, 3 << 20])   # 128 % 3 != 0
+    null_plane = _lib.PeerPlanes.make(2, 1, [1 << 20, 0])
+    p_ok, p_in_ragged = prob(256, 512), prob(12, 512, _lib.INCOMING)
+    scatter = lib.ftm_input_stage_scatter
+    assert scatter(None, fake, None, fake, ctypes.byref(planes), ctypes.byref(planes), fake, err, None) \
+        == _lib.BAD_ARGUMENT
+    assert scatter(ctypes.byref(p_ok), fake, None, fake, ctypes.byref(bad_world),
+                   ctypes.byref(bad_world), fake, err, None) == _lib.BAD_ARGUMENT
+    assert scatter(ctypes.byref(p_ok), fake, None, fake, ctypes.byref(null_plane),
+                   ctypes.byref(null_plane), fake, err, None) == _lib.BAD_ARGUMENT
+    assert scatter(ctypes.byref(p_in_ragged), fake, None, fake, ctypes.byref(planes),
+                   ctypes.byref(planes), fake, err, None) == _lib.BAD_SHAPE
+    assert scatter(ctypes.byref(p_ok), fake, None, fake, ctypes.byref(planes), ctypes.byref(planes),
+                   fake, err, None) == _lib.UNSUPPORTED_ARCH
+    cs = lib.ftm_contraction_scatter
+    assert cs(fake, fake, ctypes.byref(planes), 1, 128, 256, 512, _lib.OUTGOING, err, None) \
+        == _lib.UNSUPPORTED_ARCH
+    assert cs(fake, fake, ctypes.byref(planes), 1, 128, 200, 400, _lib.OUTGOING, err, None) \
+        == _lib.BAD_SHAPE                                  # rows % 256
+    assert cs(fake, fake, ctypes.byref(planes), 1, 128, 256, 1024, _lib.OUTGOING, err, None) \
+        == _lib.BAD_SHAPE                                  # n != P * rows
+    assert cs(fake, fake, ctypes.byref(planes), 1, 128, 256, 512, 7, err, None) == _lib.BAD_ARGUMENT
+    kb = lib.ftm_contraction_kblocked
+    assert kb(fake, fake, fake, 3, 512, 512, 100, 2, 256, err, None) == _lib.BAD_SHAPE   # k block % 64
+    assert kb(fake, fake, fake, 3, 512, 512, 256, 2, 200, err, None) == _lib.BAD_SHAPE   # x blocks
+    assert kb(None, fake, fake, 3, 512, 512, 256, 2, 256, err, None) == _lib.BAD_ARGUMENT
+    assert kb(fake, fake, fake, 3, 512, 512, 256, 2, 256, err, None) == _lib.UNSUPPORTED_ARCH

@@ -71,3 +71,21 @@ def test_row_range_and_constraints():
     assert row_range(2048, 8, 3) == (768, 1024)
     with pytest.raises(ValueError):
         row_range(100, 8, 0)
+
+
+def test_incoming_sharding_needs_a_channel_sharded_scheme():
+    """Incoming mode reduces over z rows, so an all-gather of b (outgoing's scheme) does not
+    apply; the channel-sharded schemes accept it and the default picks one."""
+    from fast_trimul_b200.distributed import RowShardedTriMul, TorchStageOps, default_scheme
+    from tests.helpers import make_layer
+    m = make_layer("incoming", True, d=128)
+    for scheme in ("allgather", "allgather_ce"):
+        with pytest.raises(NotImplementedError):
+            RowShardedTriMul(m._impl, 1, 16, chunks=1, device="cpu", z_dtype=torch.float32,
+                             ops=TorchStageOps(m._impl), scheme=scheme)
+    assert default_scheme(2, "incoming") == "alltoall_ce"
+    assert default_scheme(2, "outgoing") == "allgather_ce"
+    assert default_scheme(8, "outgoing") == "alltoall_ce"
+    with pytest.raises(ValueError):     # unknown scheme
+        RowShardedTriMul(make_layer("outgoing", True, d=128)._impl, 1, 16, chunks=1, device="cpu",
+                         z_dtype=torch.float32, ops=TorchStageOps(m._impl), scheme="unknown")

@@ -315,3 +315,31 @@ def test_c_abi_rejects_bad_arguments_before_touching_a_device():
     assert kb(fake, fake, fake, 3, 512, 512, 256, 2, 200, err, None) == _lib.BAD_SHAPE   # x blocks
     assert kb(None, fake, fake, 3, 512, 512, 256, 2, 256, err, None) == _lib.BAD_ARGUMENT
     assert kb(fake, fake, fake, 3, 512, 512, 256, 2, 256, err, None) == _lib.UNSUPPORTED_ARCH
+
+
+def test_bench_line_has_every_contract_key():
+    """bench.py's JSON line, built from a stand-in measurement on the CPU: every key the
+    contract names, the roofline fractions and vs_baseline derived consistently."""
+    import argparse
+    import json
+    import sys, os
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    args = argparse.Namespace(n=2048, gpus=1, steps=10, warmup=3, mode="outgoing")
+    res = {"ms_per_step": 3.2, "stage_ms": {"input_stage": 0.75, "contraction": 1.65, "output_stage": 0.8},
+           "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 5},
+           "e2e": {"value": 130.0, "unit": "TFLOP/s", "h2d_bytes_per_step": 1, "d2h_bytes_per_step": 1},
+           "gpu_launches": 30}
+    line = json.loads(json.dumps(bench.build_line(args, res, 1)))
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "roofline", "clocks", "e2e",
+              "gpu_launches"):
+        assert k in line, k
+    assert line["value"] == round(bench.trimul_flops(1, 2048) / 3.2e-3 / 1e12, 3)
+    rf = line["roofline"]
+    assert rf["frac"] == round(rf["achieved"] / rf["peak"], 3)
+    assert rf["bound"] == "tensor" and rf["unit"] == "TFLOP/s"
+    assert abs(rf["achieved"] - 2 * 128 * 2048 ** 3 / 1.65e-3 / 1e12) < 0.1
+    assert line["vs_baseline"] == round(line["value"] / 24.65, 2)
+    assert line["config"]["workload"].startswith("C5 outgoing")
+    assert set(line["stages"]) == {"input_stage", "contraction", "output_stage"}

@@ -343,3 +343,28 @@ def test_bench_line_has_every_contract_key():
     assert line["vs_baseline"] == round(line["value"] / 24.65, 2)
     assert line["config"]["workload"].startswith("C5 outgoing")
     assert set(line["stages"]) == {"input_stage", "contraction", "output_stage"}
+
+
+def test_c_caller_compiles_against_the_header_and_links():
+    """The boundary from plain C: tests/c_abi/abi_host_check.c includes only the public
+    header, links libfast_trimul_b200.so and checks sizes, status strings and argument
+    validation (host-side paths only; nothing is launched)."""
+    import os
+    import shutil
+    import subprocess
+    import tempfile
+    from fast_trimul_b200 import _lib
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    with tempfile.TemporaryDirectory() as tmp:
+        exe = os.path.join(tmp, "abi_host_check")
+        subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(root, "include"),
+                        os.path.join(root, "tests", "c_abi", "abi_host_check.c"),
+                        "-L", libdir, "-l:libfast_trimul_b200.so", "-Wl,-rpath," + libdir,
+                        "-o", exe], check=True, capture_output=True, text=True)
+        r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "all host-side checks passed" in r.stdout

@@ -71,6 +71,8 @@ SIGNATURES = {
     "ftm_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ftm_device_supported": (ctypes.c_int, [ctypes.c_int]),
     "ftm_last_launch_count": (ctypes.c_int, []),
+    "ftm_trimul_fwd_static_scratch": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_static_scratch_error_word": (_vp, []),
 }
 
 

@@ -33,6 +33,68 @@ def _linear(d_in, d_out):
     return lin
 
 
+class DeviceErrorWord:
+    """The sticky error word every module call on one GPU passes to its kernels.
+
+    A kernel whose bounded wait expires records `(kernel << 8) | (role << 4) | site`
+    there and drains instead of hanging. After each call an asynchronous 4-byte copy
+    moves the word into pinned host memory, followed by an event; the next call reads
+    that copy once its event has completed (`poll`, no synchronisation) and raises.
+    `check` synchronises and reads the word itself. Both clear the word when they
+    report it. Nothing is polled or recorded while the stream is being captured."""
+
+    def __init__(self, device):
+        self.device = device
+        self.dev = torch.zeros(64, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+        self.ptr = self.dev.data_ptr()
+
+    def after_launch(self):
+        if torch.cuda.is_current_stream_capturing():
+            return
+        self.host.copy_(self.dev[:1], non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record()
+
+    def _raise(self, code):
+        self.dev.zero_()
+        self.host.zero_()
+        self.event = None
+        raise _lib.NativeKernelError(
+            f"a bounded device wait expired in a native TriMul kernel (code 0x{code:x}: kernel "
+            f"{code >> 8}, role {(code >> 4) & 15}, site {code & 15}); its output is invalid")
+
+    def poll(self):
+        if self.event is None or torch.cuda.is_current_stream_capturing():
+            return
+        if self.event.query():
+            code = int(self.host[0])
+            self.event = None
+            if code:
+                self._raise(code)
+
+    def check(self):
+        torch.cuda.synchronize(self.device)
+        code = int(self.dev[0].item())
+        self.event = None
+        if code:
+            self._raise(code)
+
+
+_ERROR_WORDS = {}
+
+
+def device_error_word(device):
+    """The process-wide DeviceErrorWord of `device` (created on first use)."""
+    device = torch.device(device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    w = _ERROR_WORDS.get(key)
+    if w is None:
+        w = _ERROR_WORDS[key] = DeviceErrorWord(torch.device("cuda", key))
+    return w
+
+
 class TriangleMultiplicativeUpdateKernelFused(nn.Module):
     """Weights + mode of one TriMul layer (the reference's fused-kernel module)."""
 
@@ -123,7 +185,13 @@ class TriangleMultiplicativeUpdateKernelFused(nn.Module):
     def _forward_native(self, z, mask=None, out_dtype=None):
         """z: (B, N, N, d_z) CUDA tensor (fp16/bf16; fp32 is converted to fp16 like
         functional.py:23); mask: (B, N, N) or None. Returns z's dtype unless
-        `out_dtype` says otherwise. Mask semantics are applied inside the kernels."""
+        `out_dtype` says otherwise. Mask semantics are applied inside the kernels.
+
+        The three stages are launched through the C ABI on the current stream, with
+        a, b, x and the LayerNorm statistics in a workspace from torch's caching
+        allocator and the device error word of this GPU (`device_error_word`): a
+        bounded device wait that expired in an earlier call raises
+        `NativeKernelError` here, without a synchronisation."""
         lib = _lib.load()
         if not self.native_supported():
             raise _lib.NativeDeclined(f"native kernels need d_z == d_c == 128, got "
@@ -134,19 +202,37 @@ class TriangleMultiplicativeUpdateKernelFused(nn.Module):
         z = z.contiguous()
         if mask is not None:
             mask = mask.to(device=z.device, dtype=torch.float32).expand(z.shape[:3]).contiguous()
+        errw = device_error_word(z.device)
+        errw.poll()
         packed, _ = self.packed_params()
         prob = self.problem(z, out_dtype)
-        ws_bytes = lib.ftm_workspace_bytes(prob)
-        if ws_bytes == 0:
+        if lib.ftm_workspace_bytes(prob) == 0:
             raise _lib.NativeDeclined(f"unsupported problem {tuple(z.shape)}")
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=z.device)
+        B, N = z.shape[0], z.shape[2]
+        plane = (B * self.d_c * N * N * 2 + 255) // 256 * 256
+        ws = torch.empty(3 * plane + B * N * N * 8, dtype=torch.uint8, device=z.device)
+        base = ws.data_ptr()
+        a, b, x, zst = base, base + plane, base + 2 * plane, base + 3 * plane
         out = torch.empty(z.shape, dtype=out_dtype, device=z.device)
-        st = lib.ftm_trimul_fwd(prob, z.data_ptr(), None if mask is None else mask.data_ptr(),
-                                packed.data_ptr(), out.data_ptr(), ws.data_ptr(), ws_bytes,
-                                torch.cuda.current_stream(z.device).cuda_stream)
-        _lib.check(st, "ftm_trimul_fwd")
-        _lib.record_launches()
+        s = torch.cuda.current_stream(z.device).cuda_stream
+        mptr = None if mask is None else mask.data_ptr()
+        e = errw.ptr
+        _lib.check(lib.ftm_input_stage(prob, z.data_ptr(), mptr, packed.data_ptr(), a, b, zst, e, s),
+                   "ftm_input_stage")
+        _lib.check(lib.ftm_contraction(a, b, x, B * self.d_c, N, N, N, 1, e, s), "ftm_contraction")
+        _lib.check(lib.ftm_output_stage(prob, z.data_ptr(), mptr, x, zst, packed.data_ptr(),
+                                        out.data_ptr(), e, s), "ftm_output_stage")
+        errw.after_launch()
+        _lib.stats["calls"] += 1
+        _lib.stats["kernel_launches"] += 3
         return out
+
+    def check(self, device=None):
+        """Synchronise this layer's GPU and raise `NativeKernelError` if a bounded device
+        wait expired in any native call since the last check."""
+        dev = self.proj_a.weight.device if device is None else torch.device(device)
+        if dev.type == "cuda":
+            device_error_word(dev).check()
 
     def forward(self, z: torch.Tensor, mask: torch.Tensor = None) -> torch.Tensor:
         """The fused module's forward (used by `functional.triangle_multiplication`):

@@ -340,6 +340,23 @@ WsLayout ws_layout(const ftm_problem* p) {
 
 }  // namespace
 
+namespace ftm {
+
+int check_forward_args(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+                       const void* out) {
+  const int st = check_problem(p);
+  if (st != FTM_OK) return st;
+  if (p->rows != p->cols) return FTM_BAD_SHAPE;  // row shards go through the stage calls
+  if (!z || !packed || !out) return FTM_BAD_ARGUMENT;
+  if (!aligned16(z) || !aligned16(packed) || !aligned16(out) || (mask && !aligned16(mask)))
+    return FTM_BAD_ALIGN;
+  return FTM_OK;
+}
+
+void set_last_launch_count(int n) { g_last_launches = n; }
+
+}  // namespace ftm
+
 extern "C" {
 
 size_t ftm_packed_params_bytes(int32_t c_z, int32_t c_h) {
@@ -377,12 +394,8 @@ int* ftm_workspace_error_word(const ftm_problem* p, void* workspace) {
 int ftm_trimul_fwd(const ftm_problem* p, const void* z, const float* mask, const void* packed,
                    void* out, void* workspace, size_t workspace_bytes, ftm_stream_t stream) {
   g_last_launches = 0;
-  int st = check_problem(p);
+  int st = check_forward_args(p, z, mask, packed, out);
   if (st != FTM_OK) return st;
-  if (p->rows != p->cols) return FTM_BAD_SHAPE;  // row shards go through the stage calls
-  if (!z || !packed || !out) return FTM_BAD_ARGUMENT;
-  if (!aligned16(z) || !aligned16(packed) || !aligned16(out) || (mask && !aligned16(mask)))
-    return FTM_BAD_ALIGN;
   const WsLayout w = ws_layout(p);
   if (!workspace || workspace_bytes < w.total) return FTM_BAD_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255u) return FTM_BAD_ALIGN;

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "ftm_common.cuh"
+#include "../../include/fast_trimul_b200.h"
 
 namespace ftm {
 
@@ -86,6 +87,13 @@ cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap
                                 int out_dtype, const PosTiling& tl, int residual, int z_bf16,
                                 float eps_in, float eps_out, int* err, int grid,
                                 cudaStream_t stream);
+
+// Argument checks of a whole square forward (ftm_trimul_fwd and the static-scratch
+// entry): problem, rows == cols, non-null 16-byte-aligned z / packed / out / mask.
+int check_forward_args(const ftm_problem* p, const void* z, const float* mask, const void* packed,
+                       const void* out);
+// What ftm_last_launch_count() reports for the calling thread.
+void set_last_launch_count(int n);
 
 cudaError_t launch_pack_params(const void* const params[16], int param_is_f16, int c_z, int c_h,
                                void* packed, cudaStream_t stream);

@@ -18,7 +18,14 @@
 //
 // The device address of the array is looked up once per device, on the first call
 // made with that device current (cudaGetSymbolAddress); make that first call before
-// any stream capture.
+// any stream capture. The cached address belongs to the device's primary context: a
+// process that resets the device (cudaDeviceReset) must not call this entry point
+// afterwards, because the cached address no longer names the array.
+//
+// ftm_static_scratch_error_word() returns the device's error word inside the array,
+// for ftm_check_error: a bounded device wait that expired in a call is reported
+// there, not through the call's return value (the call returns once it has queued
+// the kernels).
 #include <mutex>
 
 #include "../../include/fast_trimul_b200.h"
@@ -53,12 +60,13 @@ void* scratch_address(int dev) {
 extern "C" int ftm_trimul_fwd_static_scratch(const ftm_problem* p, const void* z,
                                              const float* mask, const void* packed, void* out,
                                              ftm_stream_t stream) {
-  if (!p) return FTM_BAD_ARGUMENT;
-  if (p->batch < 1 || p->rows < 1 || p->cols < 1) return FTM_BAD_SHAPE;
-  if (p->rows != p->cols) return FTM_BAD_SHAPE;
+  ftm::set_last_launch_count(0);
+  // every argument is checked before anything is queued, so a rejected call leaves the
+  // shared array as it was
+  int st = ftm::check_forward_args(p, z, mask, packed, out);
+  if (st != FTM_OK) return st;
   const double positions = double(p->batch) * p->rows * p->cols;
   if (positions > double(FTM_STATIC_SCRATCH_MAX_POSITIONS)) return FTM_BAD_WORKSPACE;
-  if (p->c_z != ftm::kC || p->c_h != ftm::kC) return FTM_BAD_SHAPE;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FTM_LAUNCH_FAILED;
   if (ftm_device_supported(dev) != 1) return FTM_UNSUPPORTED_ARCH;
@@ -72,9 +80,20 @@ extern "C" int ftm_trimul_fwd_static_scratch(const ftm_problem* p, const void* z
   int* err = reinterpret_cast<int*>(base + 3 * kPlaneBytes + kStatsBytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(err, 0, sizeof(int), s) != cudaSuccess) return FTM_LAUNCH_FAILED;
-  int st = ftm_input_stage(p, z, mask, packed, a, b, zstats, err, stream);
+  st = ftm_input_stage(p, z, mask, packed, a, b, zstats, err, stream);
   if (st != FTM_OK) return st;
   st = ftm_contraction(a, b, x, p->batch * ftm::kC, p->rows, p->cols, p->cols, 1, err, stream);
   if (st != FTM_OK) return st;
-  return ftm_output_stage(p, z, mask, x, zstats, packed, out, err, stream);
+  st = ftm_output_stage(p, z, mask, x, zstats, packed, out, err, stream);
+  if (st != FTM_OK) return st;
+  ftm::set_last_launch_count(3);
+  return FTM_OK;
+}
+
+extern "C" int* ftm_static_scratch_error_word(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  unsigned char* base = static_cast<unsigned char*>(scratch_address(dev));
+  if (!base) return nullptr;
+  return reinterpret_cast<int*>(base + 3 * kPlaneBytes + kStatsBytes);
 }

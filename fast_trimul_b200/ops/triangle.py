@@ -5,9 +5,9 @@ and named loaders. The fp16 weights live in `_impl` (same parameter names as the
 reference, so state_dicts and loaders are unchanged). `forward` goes through the
 dispatcher: on a CUDA tensor the sm_100a kernels, elsewhere the torch formula.
 
-`graphed` keeps the reference's CUDA-graph capture API (static input / mask /
-output buffers, replay on every call). The native forward is three persistent
-launches, so a graph mostly saves host overhead at small N.
+`graphed(z, mask)` keeps the reference's call shape -- capture at z's shape, then
+every forward replays -- but the graph holds only the three kernel launches of a
+pre-planned forward (`plan.GraphedTriMul`); it saves host time at small N.
 """
 
 import torch
@@ -37,25 +37,22 @@ class FastTriangleMultiplication(nn.Module):
         self.backend = backend
         self._impl = TriangleMultiplicativeUpdateKernelFused(d_z, d_c, mode, residual).half()
         self._graph = None
-        self._static_in = None
-        self._static_mask = None
-        self._static_out = None
 
     # ------------------------------------------------------------------ weights
     def _load_remapped(self, remapped):
-        """Load a remapped state dict; zero biases the source omits, raise on any
-        unexpected key or missing non-bias key (ops/triangle.py:46-58)."""
-        result = self._impl.load_state_dict(remapped, strict=False)
-        if result.unexpected_keys:
-            raise KeyError(f"unexpected keys after remap: {result.unexpected_keys}")
-        missing = [k for k in result.missing_keys if not k.endswith(".bias")]
-        if missing:
-            raise KeyError(f"missing keys after remap: {missing}")
-        own = dict(self._impl.named_parameters())
-        with torch.no_grad():
-            for k in result.missing_keys:
-                own[k].zero_()
-        return result
+        """Load a state dict already renamed to this module's keys. Every weight must be
+        present; a bias the source library does not have is loaded as zeros; a key this
+        module does not know is an error (the reference's rules, ops/triangle.py:46-70)."""
+        own = self._impl.state_dict()
+        unknown = sorted(set(remapped) - set(own))
+        if unknown:
+            raise KeyError(f"unexpected keys after remap: {unknown}")
+        absent = [k for k in own if k not in remapped]
+        if any(not k.endswith(".bias") for k in absent):
+            raise KeyError(f"missing keys after remap: {[k for k in absent if not k.endswith('.bias')]}")
+        full = {k: (remapped[k] if k in remapped else torch.zeros_like(v)) for k, v in own.items()}
+        self._impl.load_state_dict(full, strict=True)
+        return _LoadResult(absent, [])
 
     def load_weights(self, state_dict, source: str):
         return self._load_remapped(get_loader(source)(dict(state_dict)))
@@ -74,29 +71,38 @@ class FastTriangleMultiplication(nn.Module):
 
     # --------------------------------------------------------------- cuda graph
     def graphed(self, z: torch.Tensor, mask: torch.Tensor = None):
-        """Capture forward at z's shape into a CUDA graph and replay it on every call
-        (inference, fixed shape), as ops/triangle.py:73-91."""
-        from ..functional import triangle_multiplication
-        stream = torch.cuda.Stream()
-        stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(stream), torch.no_grad():
-            for _ in range(3):
-                triangle_multiplication(z, self._impl, mask=mask)
-        torch.cuda.current_stream().wait_stream(stream)
-        self._static_in = z.clone()
-        self._static_mask = None if mask is None else mask.clone()
-        self._graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self._graph), torch.no_grad():
-            self._static_out = triangle_multiplication(self._static_in, self._impl,
-                                                       mask=self._static_mask)
+        """Fix the shape of z and replay the native forward from a CUDA graph on every
+        later call (inference only). The graph holds the three kernel launches and
+        nothing else; see `fast_trimul_b200.plan.GraphedTriMul`. Returns self, like the
+        reference's `graphed` (ops/triangle.py:73)."""
+        from ..plan import GraphedTriMul
+        self._graph = GraphedTriMul(self._impl, z, mask)
         return self
+
+    def graph_input(self):
+        """The tensor the captured graph reads z from (None before `graphed`). Writing
+        the next input into it in place makes a replay copy-free."""
+        return None if self._graph is None else self._graph.staging_input()
+
+    def check(self):
+        """Synchronise and raise `NativeKernelError` if a bounded device wait expired in
+        a native call of this layer since the last check."""
+        self._impl.check()
 
     # ------------------------------------------------------------------ forward
     def forward(self, z: torch.Tensor, mask: torch.Tensor = None) -> torch.Tensor:
         if self._graph is not None:
-            self._static_in.copy_(z)
-            if mask is not None and self._static_mask is not None:
-                self._static_mask.copy_(mask)
-            self._graph.replay()
-            return self._static_out
+            return self._graph.run(z, mask)
         return dispatch.run(z, mask, self._impl, prefer=self.backend)
+
+
+class _LoadResult:
+    """What `load_weights` reports: the biases filled with zeros, and no unexpected keys
+    (those raise). Same fields as torch's `_IncompatibleKeys`."""
+
+    def __init__(self, missing_keys, unexpected_keys):
+        self.missing_keys = missing_keys
+        self.unexpected_keys = unexpected_keys
+
+    def __repr__(self):
+        return f"_LoadResult(missing_keys={self.missing_keys}, unexpected_keys={self.unexpected_keys})"

@@ -189,6 +189,11 @@ int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes*
 #define FTM_STATIC_SCRATCH_MAX_POSITIONS 65536
 int ftm_trimul_fwd_static_scratch(const ftm_problem* p, const void* z, const float* mask,
                                   const void* packed, void* out, ftm_stream_t stream);
+/* The current device's error word inside that array (NULL if its address cannot be
+ * looked up), for ftm_check_error after ftm_trimul_fwd_static_scratch calls: the word
+ * is cleared at the start of each call, so check it before the next call. No
+ * counterpart in the reference. */
+int* ftm_static_scratch_error_word(void);
 
 /* ---- status -------------------------------------------------------------- */
 /* Synchronise `stream`, read the device error word of a workspace (or any err_word

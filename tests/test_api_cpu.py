@@ -5,6 +5,7 @@ against this package's implementation of the same interface."""
 import sys
 import types
 
+import numpy as np
 import pytest
 import torch
 
@@ -368,3 +369,21 @@ def test_c_caller_compiles_against_the_header_and_links():
         r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "all host-side checks passed" in r.stdout
+
+
+@pytest.mark.parametrize("mode", ["outgoing", "incoming"])
+@pytest.mark.parametrize("residual", [True, False])
+def test_parity_rows_checker_matches_oracle(mode, residual):
+    """The fp32 row-sampled checker used at N = 2048 (fast_trimul_b200.parity) equals
+    the oracle on the rows it evaluates."""
+    from fast_trimul_b200.parity import reference_rows, sample_rows
+    from tests.helpers import make_layer, make_mask, oracle_out
+    m = make_layer(mode, residual, d=32)
+    gen = torch.Generator().manual_seed(4)
+    B, N = 2, 24
+    z = torch.randn(B, N, N, 32, generator=gen).to(torch.bfloat16)
+    mask = make_mask("pad", B, N, gen)
+    rows = sample_rows(N, 5)
+    got = reference_rows(m._impl, z, mask, rows, chunk_rows=7)
+    ref = oracle_out(m, z, mask)[:, rows]
+    assert np.abs(got.numpy() - ref).max() < 1e-4

@@ -76,6 +76,32 @@ def test_native_c3_shape(mode):
 
 
 @needs_gpu
+@pytest.mark.parametrize("mode,mkind", [("outgoing", None), ("incoming", None),
+                                        ("outgoing", "tail"), ("incoming", "pad")])
+def test_native_c5_n2048(mode, mkind):
+    """Config C5, the size every benchmark number is quoted on: B=1, N=2048, bf16
+    z ~ N(0,1), random-init weights (all-ones mask as in C5, plus masked variants).
+    The checker is the fp32 formula of the reference's torch path evaluated on 24 rows
+    spread over the output (fast_trimul_b200.parity, pinned to the oracle by
+    test_api_cpu.py::test_parity_rows_checker_matches_oracle); the full forward on
+    the host would take minutes."""
+    from fast_trimul_b200.parity import error_metrics, reference_rows, sample_rows
+    m = make_layer(mode, True, ln_noise=False).cuda()
+    N = 2048
+    gen = torch.Generator(device="cuda").manual_seed(51)
+    z = torch.randn(1, N, N, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    mask = make_mask(mkind, 1, N, torch.Generator().manual_seed(52))
+    mask = torch.ones(1, N, N) if mask is None else mask
+    mask = mask.cuda()
+    out = _native(m, z, mask)
+    rows = sample_rows(N, 24)
+    ref = reference_rows(m._impl, z, mask, rows)
+    max_abs, mean_rel = error_metrics(out[:, rows], ref)
+    assert torch.isfinite(out).all()
+    assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (max_abs, mean_rel)
+
+
+@needs_gpu
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
 def test_half_outputs(out_dtype):
     m = make_layer("outgoing", True).cuda()

@@ -5,8 +5,9 @@ device-memory budget at start-up, or that must not call cudaMalloc mid-run becau
 can synchronise the device. Its scratch is a device array built into the library.
 These tests call it through the C ABI twice in a row (different inputs, so stale
 contents from the first call would show) and compare each result with ftm_trimul_fwd
-on the same inputs, within the tolerance the other GPU tests use. The file name makes
-pytest collect it last.
+on the same inputs. Both run the same three kernels on the same inputs, so the results
+must be bit-identical (torch.equal): any tolerance would hide a stale-scratch or offset
+bug smaller than it. The file name makes pytest collect it last.
 """
 
 import ctypes
@@ -14,7 +15,7 @@ import ctypes
 import pytest
 import torch
 
-from tests.helpers import MAX_ABS, make_layer, make_mask
+from tests.helpers import make_layer, make_mask
 
 pytestmark = pytest.mark.gpu
 
@@ -26,6 +27,13 @@ def _bind(lib):
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p] * 6
     return fn
+
+
+def _error_word(lib):
+    fn = lib.ftm_static_scratch_error_word
+    fn.restype = ctypes.c_void_p
+    fn.argtypes = []
+    return fn()
 
 
 def _with_workspace(lib, m, z, mask, out_dtype):
@@ -59,9 +67,12 @@ def test_static_scratch_matches_workspace_path(mode):
         st = fn(ctypes.addressof(prob), z.data_ptr(), mask.data_ptr(), packed.data_ptr(),
                 got.data_ptr(), torch.cuda.current_stream().cuda_stream)
         assert st == 0, _lib.status_string(st)
-        torch.cuda.synchronize()
-        diff = (got - want).abs().max().item()
-        assert diff <= MAX_ABS, (call, diff)
+        assert lib.ftm_last_launch_count() == 3
+        errw = _error_word(lib)
+        assert errw
+        s = torch.cuda.current_stream().cuda_stream
+        assert lib.ftm_check_error(errw, None, s) == _lib.OK
+        assert torch.equal(got, want), (call, (got - want).abs().max().item())
 
 
 @needs_gpu
@@ -75,3 +86,21 @@ def test_static_scratch_rejects_oversized_problem():
     st = fn(ctypes.addressof(prob), z.data_ptr(), None, z.data_ptr(), z.data_ptr(),
             torch.cuda.current_stream().cuda_stream)
     assert st == _lib.BAD_WORKSPACE
+
+
+@needs_gpu
+def test_static_scratch_rejects_bad_arguments_before_queueing():
+    """Null or misaligned buffers are rejected up front, with no launch."""
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    fn = _bind(lib)
+    m = make_layer("outgoing", True).cuda()
+    packed, _ = m._impl.packed_params()
+    z = torch.randn(1, 64, 64, 128, device="cuda").to(torch.bfloat16)
+    out = torch.empty(z.shape, dtype=torch.float32, device="cuda")
+    prob = m._impl.problem(z, torch.float32)
+    s = torch.cuda.current_stream().cuda_stream
+    assert fn(ctypes.addressof(prob), z.data_ptr(), None, packed.data_ptr(), None, s) == _lib.BAD_ARGUMENT
+    assert fn(ctypes.addressof(prob), z.data_ptr(), None, packed.data_ptr(), out.data_ptr() + 4,
+              s) == _lib.BAD_ALIGN
+    assert lib.ftm_last_launch_count() == 0

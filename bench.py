@@ -811,6 +811,10 @@ def build_line(args, res, world):
         line["trunk"] = res["trunk"]
     if res.get("comm"):
         line["comm"] = res["comm"]
+    if res.get("trace"):
+        line["trace"] = res["trace"]
+    if res.get("stage_note"):
+        line["stages_note"] = res["stage_note"]
     for key in ("parity", "contraction_n1024"):
         if res.get(key):
             line[key] = res[key]
@@ -831,10 +835,17 @@ def main():
                     help="reference arm: skip the one full-size CPU forward")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU kernels (reference_gpu key)")
+    ap.add_argument("--trace", action="store_true",
+                    help="N>1: add the device-clock timeline of one forward per rank (trace key)")
+    ap.add_argument("--row-chunks", type=int, default=None,
+                    help="input-stage row chunks of the native sharded pipeline (N>1)")
     ap.add_argument("--chunks", type=int, default=None,
                     help="channel chunks of the exchange (N>1; default 4 for all-gather, 2 for all-to-all)")
-    ap.add_argument("--scheme", default=None, choices=["allgather", "alltoall", "allgather_ce", "alltoall_ce", "fused"],
-                    help="multi-GPU exchange (default: allgather_ce for 2 GPUs, alltoall_ce for more)")
+    ap.add_argument("--scheme", default=None,
+                    choices=["p2p_allgather", "p2p_alltoall", "allgather", "alltoall", "allgather_ce",
+                             "alltoall_ce", "fused"],
+                    help="multi-GPU exchange (default: the native pipeline, p2p_allgather at 2 GPUs "
+                         "in outgoing mode, p2p_alltoall otherwise)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="N",
                     help="run a few plain forwards at this N (for ncu captures) and exit")
     ap.add_argument("--mode", default="outgoing", choices=["outgoing", "incoming"])

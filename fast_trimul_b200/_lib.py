@@ -47,6 +47,34 @@ class PeerPlanes(ctypes.Structure):
         return pp
 
 
+SHARD_ALLTOALL, SHARD_ALLGATHER = 0, 1
+SHARD_MAX_ROW_CHUNKS = 8
+SHARD_FLAG_WORDS = 256
+SHARD_BUF_LOCAL, SHARD_BUF_ZSTATS, SHARD_BUF_XBLOCKS, SHARD_BUF_RECV, SHARD_BUF_XPLANE, \
+    SHARD_BUF_FLAGS = range(6)
+
+
+class ShardConfig(ctypes.Structure):
+    """Mirror of ftm_shard_config."""
+    _fields_ = [("world", _i32), ("rank", _i32), ("scheme", _i32), ("row_chunks", _i32),
+                ("shard", Problem), ("packed", _vp), ("a_local", _vp), ("b_local", _vp),
+                ("zstats", _vp), ("x_blocks", _vp), ("err_word", _vp),
+                ("recv_a", _vp * MAX_RANKS), ("recv_b", _vp * MAX_RANKS),
+                ("x_plane", _vp * MAX_RANKS), ("flags", _vp * MAX_RANKS)]
+
+
+class ContractionLayout(ctypes.Structure):
+    """Mirror of ftm_contraction_layout."""
+    _i64 = ctypes.c_int64
+    _fields_ = [("L", _i32), ("m", _i32), ("n", _i32), ("k", _i32), ("k_per_block", _i32),
+                ("a", _vp), ("a_rows_per_block", _i32), ("a_block_stride", _i64),
+                ("a_l_stride", _i64), ("a_row_stride", _i64), ("a_kblock_stride", _i64),
+                ("b", _vp), ("b_rows_per_block", _i32), ("b_block_stride", _i64),
+                ("b_l_stride", _i64), ("b_row_stride", _i64), ("b_kblock_stride", _i64),
+                ("x", _vp), ("x_rows_per_block", _i32), ("x_block_stride", _i64),
+                ("x_l_stride", _i64), ("x_row_stride", _i64)]
+
+
 _PP = ctypes.POINTER(Problem)
 _IP = ctypes.POINTER(ctypes.c_int)
 _PPL = ctypes.POINTER(PeerPlanes)
@@ -72,6 +100,12 @@ SIGNATURES = {
     "ftm_device_supported": (ctypes.c_int, [ctypes.c_int]),
     "ftm_last_launch_count": (ctypes.c_int, []),
     "ftm_trimul_fwd_static_scratch": (ctypes.c_int, [_PP, _vp, _vp, _vp, _vp, _vp]),
+    "ftm_contraction_general": (ctypes.c_int, [ctypes.POINTER(ContractionLayout), _vp, _vp]),
+    "ftm_shard_buffer_bytes": (_sz, [ctypes.POINTER(ShardConfig), ctypes.c_int]),
+    "ftm_shard_plan_create": (ctypes.c_int, [ctypes.POINTER(ShardConfig), ctypes.POINTER(_vp)]),
+    "ftm_shard_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "ftm_shard_plan_destroy": (None, [_vp]),
+    "ftm_shard_set_trace": (ctypes.c_int, [_vp, _vp]),
     "ftm_static_scratch_error_word": (_vp, []),
 }
 

@@ -207,20 +207,98 @@ bool use_pair_contraction() {
   return !(v && strcmp(v, "single") == 0);
 }
 
+// 5-D operand map (k in k block, row in row block, l, row block, k block) of one
+// contraction operand; strides in elements. A single row / k block gets a stride that
+// spans everything before it.
+bool make_operand_map(CUtensorMap* m, const void* base, int L, int rows, int rpb, int k, int kpb,
+                      long long bs, long long ls, long long rs, long long kbs) {
+  const uint64_t nrb = uint64_t((rows + rpb - 1) / rpb), nkb = uint64_t(k / kpb);
+  if (nrb == 1) bs = ls * L;
+  if (nkb == 1) kbs = bs * static_cast<long long>(nrb);
+  const uint64_t dims[5] = {uint64_t(kpb), uint64_t(rpb), uint64_t(L), nrb, nkb};
+  const uint64_t strides[4] = {uint64_t(rs) * 2, uint64_t(ls) * 2, uint64_t(bs) * 2, uint64_t(kbs) * 2};
+  const uint32_t box[5] = {kCtBK, 128u, 1, 1, 1};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, base, dims, strides, box);
+}
+
+// Checks of a general layout (see ftm_contraction_layout); normalises single-block
+// sizes. Returns an ftm_status.
+int check_layout(ftm_contraction_layout* d) {
+  if (!d || !d->a || !d->b || !d->x) return FTM_BAD_ARGUMENT;
+  if (d->L < 1 || d->m < 1 || d->n < 1 || d->k < 1) return FTM_BAD_SHAPE;
+  if (d->n % 8 != 0) return FTM_BAD_SHAPE;
+  if (d->k_per_block <= 0 || d->k_per_block >= d->k) d->k_per_block = d->k;
+  if (d->k_per_block < d->k && (d->k % d->k_per_block != 0 || d->k_per_block % kCtBK != 0))
+    return FTM_BAD_SHAPE;
+  if (d->a_rows_per_block <= 0 || d->a_rows_per_block >= d->m) d->a_rows_per_block = d->m;
+  else if (d->m % d->a_rows_per_block != 0 || d->a_rows_per_block % 128 != 0) return FTM_BAD_SHAPE;
+  if (d->b_rows_per_block <= 0 || d->b_rows_per_block >= d->n) d->b_rows_per_block = d->n;
+  else if (d->n % d->b_rows_per_block != 0 || d->b_rows_per_block % 128 != 0) return FTM_BAD_SHAPE;
+  if (d->x_rows_per_block <= 0 || d->x_rows_per_block >= d->m) d->x_rows_per_block = d->m;
+  else if (d->m % d->x_rows_per_block != 0) return FTM_BAD_SHAPE;
+  const long long strides[] = {d->a_l_stride, d->a_row_stride, d->b_l_stride, d->b_row_stride,
+                               d->x_l_stride, d->x_row_stride};
+  for (long long s : strides)
+    if (s <= 0 || s % 8 != 0) return FTM_BAD_ALIGN;
+  const long long opt[] = {d->a_block_stride, d->a_kblock_stride, d->b_block_stride,
+                           d->b_kblock_stride, d->x_block_stride};
+  for (long long s : opt)
+    if (s < 0 || s % 8 != 0) return FTM_BAD_ALIGN;
+  if (d->a_row_stride < d->k_per_block || d->b_row_stride < d->k_per_block) return FTM_BAD_SHAPE;
+  if (!aligned16(d->a) || !aligned16(d->b) || !aligned16(d->x)) return FTM_BAD_ALIGN;
+  return FTM_OK;
+}
+
+int stage_contract_general(const ftm_contraction_layout& d, int* err, cudaStream_t stream, int dev,
+                           const XDest* xdest = nullptr) {
+  CUtensorMap amap, bmap;
+  if (!make_operand_map(&amap, d.a, d.L, d.m, d.a_rows_per_block, d.k, d.k_per_block,
+                        d.a_block_stride, d.a_l_stride, d.a_row_stride, d.a_kblock_stride) ||
+      !make_operand_map(&bmap, d.b, d.L, d.n, d.b_rows_per_block, d.k, d.k_per_block,
+                        d.b_block_stride, d.b_l_stride, d.b_row_stride, d.b_kblock_stride))
+    return FTM_LAUNCH_FAILED;
+  CtLayout lay{d.a_rows_per_block, d.b_rows_per_block, d.k_per_block, d.x_rows_per_block,
+               d.x_block_stride, d.x_l_stride, d.x_row_stride};
+  const cudaError_t e = launch_contraction_pair(amap, bmap, static_cast<__half*>(d.x), d.L, d.m,
+                                                d.n, d.k, lay, err, sm_count(dev), stream, xdest);
+  return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
+}
+
+// A (and X) as a_blocks row blocks of (L, a_rpb, k), B as `blocks` row blocks of
+// (L, rpb, k): the layouts of ftm_contraction_blocked.
+ftm_contraction_layout blocked_layout(const void* A, const void* B, void* X, int L, int a_rpb,
+                                      int a_blocks, int k, int rpb, int blocks) {
+  ftm_contraction_layout d{};
+  const long long m = static_cast<long long>(a_rpb) * a_blocks, n = static_cast<long long>(rpb) * blocks;
+  d.L = L; d.m = static_cast<int>(m); d.n = static_cast<int>(n); d.k = k; d.k_per_block = k;
+  d.a = A; d.a_rows_per_block = a_rpb;
+  d.a_row_stride = k; d.a_l_stride = static_cast<long long>(a_rpb) * k;
+  d.a_block_stride = d.a_l_stride * L;
+  d.b = B; d.b_rows_per_block = rpb;
+  d.b_row_stride = k; d.b_l_stride = static_cast<long long>(rpb) * k;
+  d.b_block_stride = d.b_l_stride * L;
+  d.x = X; d.x_rows_per_block = a_rpb;
+  d.x_row_stride = n; d.x_l_stride = a_rpb * n; d.x_block_stride = d.x_l_stride * L;
+  return d;
+}
+
 int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int a_blocks, int k,
                    int rpb, int blocks, int* err, cudaStream_t stream, int dev,
                    const XDest* xdest = nullptr) {
-  const bool pair = use_pair_contraction() || a_blocks > 1 || xdest != nullptr;
+  // the single-CTA kernel reads B in 256-row tiles: blocked B of 128-row blocks and
+  // blocked A always go to the pair kernel
+  const bool pair = use_pair_contraction() || a_blocks > 1 || xdest != nullptr ||
+                    (blocks > 1 && rpb % kCtBN != 0);
   const int m = a_rpb * a_blocks;
-  CUtensorMap amap, bmap;
+  const int n = rpb * blocks;
   if (pair) {
-    const uint64_t dims[4] = {uint64_t(k), uint64_t(a_rpb), uint64_t(L), uint64_t(a_blocks)};
-    const uint64_t strides[3] = {uint64_t(k) * 2, uint64_t(a_rpb) * k * 2,
-                                 uint64_t(L) * a_rpb * k * 2};
-    const uint32_t box[4] = {kCtBK, kCtBM, 1, 1};
-    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, A, dims, strides, box))
-      return FTM_LAUNCH_FAILED;
-  } else {
+    ftm_contraction_layout d = blocked_layout(A, B, X, L, a_rpb, a_blocks, k, rpb, blocks);
+    const int st = check_layout(&d);
+    if (st != FTM_OK) return st;
+    return stage_contract_general(d, err, stream, dev, xdest);
+  }
+  CUtensorMap amap, bmap;
+  {
     const uint64_t dims[3] = {uint64_t(k), uint64_t(m), uint64_t(L)};
     const uint64_t strides[2] = {uint64_t(k) * 2, uint64_t(m) * k * 2};
     const uint32_t box[3] = {kCtBK, kCtBM, 1};
@@ -231,20 +309,14 @@ int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int 
     const uint64_t dims[4] = {uint64_t(k), uint64_t(rpb), uint64_t(L), uint64_t(blocks)};
     const uint64_t strides[3] = {uint64_t(k) * 2, uint64_t(rpb) * k * 2,
                                  uint64_t(L) * rpb * k * 2};
-    const uint32_t box[4] = {kCtBK, pair ? 128u : uint32_t(kCtBN), 1, 1};
+    const uint32_t box[4] = {kCtBK, uint32_t(kCtBN), 1, 1};
     if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, B, dims, strides, box))
       return FTM_LAUNCH_FAILED;
   }
-  const int n = rpb * blocks;
-  cudaError_t e;
-  if (pair) {
-    e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, a_rpb, err,
-                                sm_count(dev), stream, xdest);
-  } else {
-    const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
-    const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
-    e = launch_contraction(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err, grid, stream);
-  }
+  const long tiles = long(L) * ((m + kCtBM - 1) / kCtBM) * ((n + kCtBN - 1) / kCtBN);
+  const int grid = tiles < sm_count(dev) ? int(tiles) : sm_count(dev);
+  const cudaError_t e =
+      launch_contraction(amap, bmap, static_cast<__half*>(X), L, m, n, k, rpb, err, grid, stream);
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 
@@ -254,27 +326,17 @@ int stage_contract(const void* A, const void* B, void* X, int L, int a_rpb, int 
 int stage_contract_kblocked(const void* A, const void* B, void* X, int L, int m, int n, int k_rpb,
                             int k_blocks, int x_rpb, int* err, cudaStream_t stream, int dev,
                             const XDest* xdest = nullptr) {
-  CUtensorMap amap, bmap;
-  {
-    const uint64_t dims[4] = {uint64_t(k_rpb), uint64_t(m), uint64_t(L), uint64_t(k_blocks)};
-    const uint64_t strides[3] = {uint64_t(k_rpb) * 2, uint64_t(m) * k_rpb * 2,
-                                 uint64_t(L) * m * k_rpb * 2};
-    const uint32_t box[4] = {kCtBK, kCtBM, 1, 1};
-    if (!make_map(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, A, dims, strides, box))
-      return FTM_LAUNCH_FAILED;
-  }
-  {
-    const uint64_t dims[4] = {uint64_t(k_rpb), uint64_t(n), uint64_t(L), uint64_t(k_blocks)};
-    const uint64_t strides[3] = {uint64_t(k_rpb) * 2, uint64_t(n) * k_rpb * 2,
-                                 uint64_t(L) * n * k_rpb * 2};
-    const uint32_t box[4] = {kCtBK, 128u, 1, 1};
-    if (!make_map(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, B, dims, strides, box))
-      return FTM_LAUNCH_FAILED;
-  }
-  const cudaError_t e = launch_contraction_pair(amap, bmap, static_cast<__half*>(X), L, m, n,
-                                                k_rpb * k_blocks, n, m, err, sm_count(dev), stream,
-                                                xdest, k_rpb, x_rpb);
-  return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
+  ftm_contraction_layout d{};
+  d.L = L; d.m = m; d.n = n; d.k = k_rpb * k_blocks; d.k_per_block = k_rpb;
+  d.a = A; d.a_rows_per_block = m; d.a_row_stride = k_rpb;
+  d.a_l_stride = static_cast<long long>(m) * k_rpb; d.a_kblock_stride = d.a_l_stride * L;
+  d.b = B; d.b_rows_per_block = n; d.b_row_stride = k_rpb;
+  d.b_l_stride = static_cast<long long>(n) * k_rpb; d.b_kblock_stride = d.b_l_stride * L;
+  d.x = X; d.x_rows_per_block = x_rpb; d.x_row_stride = n;
+  d.x_l_stride = static_cast<long long>(x_rpb) * n; d.x_block_stride = d.x_l_stride * L;
+  const int st = check_layout(&d);
+  if (st != FTM_OK) return st;
+  return stage_contract_general(d, err, stream, dev, xdest);
 }
 
 int stage_out(const ftm_problem* p, const void* z, const float* mask, const void* x_cm,
@@ -448,7 +510,7 @@ int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
       b_blocks < 1)
     return FTM_BAD_SHAPE;
   if (k % 8 != 0 || (b_rows_per_block * b_blocks) % 8 != 0) return FTM_BAD_SHAPE;
-  if (b_blocks > 1 && b_rows_per_block % kCtBN != 0) return FTM_BAD_SHAPE;
+  if (b_blocks > 1 && b_rows_per_block % 128 != 0) return FTM_BAD_SHAPE;
   if (a_blocks > 1 && a_rows_per_block % kCtBM != 0) return FTM_BAD_SHAPE;
   if (!aligned16(A) || !aligned16(B) || !aligned16(X)) return FTM_BAD_ALIGN;
   int dev;
@@ -534,6 +596,20 @@ int ftm_contraction_kblocked(const void* A, const void* B, void* X, int32_t L, i
   const int st = stage_contract_kblocked(A, B, X, L, m, n, k_rows_per_block, k_blocks,
                                          x_rows_per_block, err_word,
                                          reinterpret_cast<cudaStream_t>(stream), dev);
+  if (st == FTM_OK) g_last_launches = 1;
+  return st;
+}
+
+int ftm_contraction_general(const ftm_contraction_layout* layout, int* err_word,
+                            ftm_stream_t stream) {
+  g_last_launches = 0;
+  if (!layout || !err_word) return FTM_BAD_ARGUMENT;
+  ftm_contraction_layout d = *layout;
+  int st = check_layout(&d);
+  if (st != FTM_OK) return st;
+  int dev;
+  if (!arch_ok(&dev)) return FTM_UNSUPPORTED_ARCH;
+  st = stage_contract_general(d, err_word, reinterpret_cast<cudaStream_t>(stream), dev);
   if (st == FTM_OK) g_last_launches = 1;
   return st;
 }

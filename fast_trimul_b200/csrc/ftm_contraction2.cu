@@ -73,12 +73,13 @@ __device__ __forceinline__ void remote_arrive(uint32_t cl_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
                : "memory");
 }
-__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cl, void* dst,
-                                                 int c0, int c1, int c2, int c3) {
+// operand tiles: (k within its k block, row within its row block, l, row block, k block)
+__device__ __forceinline__ void tma_load_5d_pair(const CUtensorMap* map, uint32_t bar_cl, void* dst,
+                                                 int c0, int c1, int c2, int c3, int c4) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
 __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
@@ -101,8 +102,7 @@ template <int NH>
 __global__ void __launch_bounds__(kThreads, 1)
 contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
                         const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
-                        int M, int N, int K, int rows_per_block, int a_rows_per_block,
-                        int k_rows_per_block, int x_rows_per_block, int* err, const XDest xd) {
+                        int M, int N, int K, const CtLayout lay, int* err, const XDest xd) {
   using Cfg = PairCfg<NH>;
   constexpr int kStages = Cfg::kStages, kStageBytes = Cfg::kStageBytes, kAcc = Cfg::kAcc;
   constexpr int kAccCols = Cfg::kAccCols;
@@ -168,14 +168,13 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         const int r = t - l * per_l;
         const int tm = r / tiles_n, tn = r - (r / tiles_n) * tiles_n;
         const int i0 = tm * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int ablk = i0 / a_rows_per_block, ail = i0 - ablk * a_rows_per_block;
-        int bblk[NH], bjl[NH], bj0[NH];
+        const int ablk = i0 / lay.a_rpb, ail = i0 - ablk * lay.a_rpb;
+        int bblk[NH], bjl[NH];
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
           const int j0 = (tn * NH + h) * 2 * kBN + static_cast<int>(rank) * kBN;
-          bj0[h] = j0;
-          bblk[h] = j0 / rows_per_block;
-          bjl[h] = j0 - bblk[h] * rows_per_block;
+          bblk[h] = j0 / lay.b_rpb;
+          bjl[h] = j0 - bblk[h] * lay.b_rpb;
         }
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[st], ph ^ 1, err, err_code(KERNEL_CONTRACT, ROLE_PRODUCER, 2))) {
@@ -185,18 +184,16 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
           uint8_t* sa = smem + st * kStageBytes;
           const uint32_t fb = cluster_addr(&full[st], 0);
           if (leader) mbar_arrive_expect_tx(&full[st], 2 * kStageBytes);
-          // k split into blocks (one per source rank: A and B are [k block][l][row][k
-          // in block]) or contiguous; rows of A / B split into row blocks otherwise
+          // rows of A / B may be split into row blocks and k into k blocks (each 64-wide
+          // k step lies inside one k block): 5-D coordinates
+          // (k in block, row in block, l, row block, k block)
           const int kg = kb * kBK;
-          const int kblk = k_rows_per_block ? kg / k_rows_per_block : 0;
-          const int kc = k_rows_per_block ? kg - kblk * k_rows_per_block : kg;
-          tma_load_4d_pair(&amap, fb, sa, kc, k_rows_per_block ? i0 : ail, l,
-                           k_rows_per_block ? kblk : ablk);
+          const int kblk = kg / lay.k_rpb;
+          const int kc = kg - kblk * lay.k_rpb;
+          tma_load_5d_pair(&amap, fb, sa, kc, ail, l, ablk, kblk);
 #pragma unroll
           for (int h = 0; h < NH; ++h)
-            tma_load_4d_pair(&bmap, fb, sa + kATile + h * kBTile, kc,
-                             k_rows_per_block ? bj0[h] : bjl[h], l,
-                             k_rows_per_block ? kblk : bblk[h]);
+            tma_load_5d_pair(&bmap, fb, sa + kATile + h * kBTile, kc, bjl[h], l, bblk[h], kblk);
           ++issued;
           if (++st == kStages) {
             st = 0;
@@ -273,14 +270,14 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
         break;
       tc_fence_after();
       const int i = tm * 2 * kBM + static_cast<int>(rank) * kBM + sub * 32 + lane;
-      // X rows are stored in blocks of a_rows_per_block like A: [block][l][row][col],
-      // or -- scattered -- each block straight into its owner's channel-major plane
-      const int xb = i / x_rows_per_block, xi = i - xb * x_rows_per_block;
+      // X rows are stored in row blocks with the strides of `lay`, or -- scattered --
+      // each block straight into its owner's channel-major plane
+      const int xb = i / lay.x_rpb, xi = i - xb * lay.x_rpb;
       __half* xrow =
           xd.enabled
               ? xd.base[xb] + ((static_cast<size_t>(l / xd.lq) * xd.c_total + xd.chan_off + l % xd.lq) *
-                                   x_rows_per_block + xi) * N
-              : X + ((static_cast<size_t>(xb) * L + l) * x_rows_per_block + xi) * N;
+                                   lay.x_rpb + xi) * N
+              : X + xb * lay.x_bs + l * lay.x_ls + xi * lay.x_rs;
       // 16-column chunks, the TMEM load of chunk ch + 1 in flight while chunk ch is
       // converted and stored
       uint32_t va[2][16];
@@ -335,11 +332,8 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
 }  // namespace
 
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
-                                    int L, int M, int N, int K, int rows_per_block,
-                                    int a_rows_per_block, int* err,
-                                    int num_sms, cudaStream_t stream, const XDest* xdest,
-                                    int k_rows_per_block, int x_rows_per_block) {
-  if (x_rows_per_block <= 0) x_rows_per_block = a_rows_per_block;
+                                    int L, int M, int N, int K, const CtLayout& lay, int* err,
+                                    int num_sms, cudaStream_t stream, const XDest* xdest) {
   XDest xd{};
   if (xdest) xd = *xdest;
   // FTM_CT_NH=2 selects the 256 x 512 tile variant
@@ -362,8 +356,7 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, amap, bmap, X, L, M, N, K, rows_per_block,
-                           a_rows_per_block, k_rows_per_block, x_rows_per_block, err, xd);
+    e = cudaLaunchKernelEx(&cfg, kern, amap, bmap, X, L, M, N, K, lay, err, xd);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };

@@ -74,11 +74,21 @@ struct XDest {
   int enabled, lq, c_total, chan_off;
 };
 
+// Layout of the CTA-pair contraction (fp16 elements). A and B are read through 5-D
+// tensor maps (k in k block, row in row block, l, row block, k block); the kernel
+// needs only the block sizes to form coordinates. X row i of channel l is stored at
+// X + (i / x_rpb) * x_bs + l * x_ls + (i % x_rpb) * x_rs.
+struct CtLayout {
+  int a_rpb, b_rpb;   // rows per row block of A, B
+  int k_rpb;          // k per k block (K when k is not split; a multiple of 64 otherwise)
+  int x_rpb;          // rows per row block of X
+  long long x_bs, x_ls, x_rs;
+};
+
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
-                                    int L, int M, int N, int K, int rows_per_block,
-                                    int a_rows_per_block, int* err, int num_sms,
-                                    cudaStream_t stream, const XDest* xdest = nullptr,
-                                    int k_rows_per_block = 0, int x_rows_per_block = 0);
+                                    int L, int M, int N, int K, const CtLayout& lay, int* err,
+                                    int num_sms, cudaStream_t stream,
+                                    const XDest* xdest = nullptr);
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
                                 const CUtensorMap& wmap, const CUtensorMap& omap,

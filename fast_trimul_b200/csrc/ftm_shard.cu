@@ -1,0 +1,467 @@
+// Row-sharded multi-GPU forward: the native pipeline behind ftm_shard_forward.
+//
+// Rank r owns R = N / P consecutive rows of z (and of the output). The input stage runs
+// on the local rows in `row_chunks` launches; as each chunk finishes, the copy engines
+// push its pieces to the ranks that need them, straight into their receive windows over
+// NVLink (CUDA IPC mappings), and a one-thread kernel on the same copy stream raises a
+// flag word in the receiver's memory. Receivers wait for their flags with a bounded
+// device-side wait kernel -- no NCCL call and no host synchronisation on the data path.
+//
+//   alltoall (both modes): chunk r's channel shard q (128 / P channels) goes to rank q.
+//     Rank q contracts its channels over all N rows, one row owner at a time (owner
+//     me + 1 first, itself last), and the x block of each owner is pushed back to that
+//     owner's x plane as soon as it is done. Bytes each rank sends per forward:
+//     3 (P - 1) / P^2 of the full a/b/x plane.
+//   allgather (outgoing): chunk r's b goes to every rank; each rank contracts its own
+//     rows against its own b at once and against each arriving chunk of a peer's b.
+//     Bytes sent: (P - 1) / P of the b plane; fewer than alltoall at P = 2.
+//
+// Buffer reuse across forwards (no extra barrier): receive windows are double-buffered
+// by forward parity. A rank pushes forward t + 1 into a peer's slot only after its own
+// output stage of forward t, which waited for data that the peer produced after all of
+// its forward t - 1 work, so the slot of t - 1 is no longer read. x planes and local
+// buffers are ordered by events between the compute and copy streams. Flags carry the
+// forward's epoch (monotonic), so they never need resetting.
+//
+// Every wait is bounded (FTM_SHARD_WAIT_NS); an expired wait records
+// (KERNEL_EXCHANGE << 8) | (kind << 4) | 1 in the error word and lets the forward run on
+// (its output is then invalid; the caller reads the word with ftm_check_error).
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "../../include/fast_trimul_b200.h"
+#include "ftm_kernels.h"
+
+#ifndef FTM_SHARD_WAIT_NS
+#define FTM_SHARD_WAIT_NS 20000000000ull  // 20 s: ranks may start a forward seconds apart
+#endif
+
+namespace ftm {
+namespace {
+
+constexpr int KERNEL_EXCHANGE = 5;
+constexpr int kFlagAB = 0;                       // [src][chunk] a/b (or b) arrived
+constexpr int kFlagX = FTM_MAX_RANKS * FTM_SHARD_MAX_ROW_CHUNKS;   // [src] x block arrived
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until flags[idx[i]] >= epoch for every i < count (one warp, bounded).
+struct FlagList {
+  int idx[FTM_MAX_RANKS * FTM_SHARD_MAX_ROW_CHUNKS];
+  int count;
+};
+
+__global__ void wait_flags_kernel(const int* flags, const FlagList list, int epoch, int* err,
+                                  int code) {
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  for (int i = threadIdx.x; ok && i < list.count; i += 32) {
+    const int* f = flags + list.idx[i];
+    while (ld_acquire_sys(f) < epoch) {
+      if (globaltimer_ns() - t0 > FTM_SHARD_WAIT_NS) {
+        atomicCAS(err, 0, code);
+        ok = false;
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  __syncwarp();
+  __threadfence();
+}
+
+// Raise one flag word (usually in a peer's memory) to `epoch`, after everything queued
+// before this launch on its stream -- the copies it announces -- has completed.
+__global__ void signal_kernel(int* flag, int epoch) {
+  __threadfence_system();
+  st_release_sys(flag, epoch);
+}
+
+// Trace point (only when a trace buffer is configured): records the device clock when
+// everything queued before it on its stream has finished.
+__global__ void mark_kernel(long long* trace, int slot, int tag) {
+  trace[2 * slot] = static_cast<long long>(globaltimer_ns());
+  trace[2 * slot + 1] = tag;
+}
+
+}  // namespace
+}  // namespace ftm
+
+using namespace ftm;
+
+struct ftm_shard_plan {
+  ftm_shard_config cfg;
+  int P, me, RC, rc, R, N, B, L, lq, dev;
+  size_t unit;              // fp16 elements of one channel of one chunk (rc * N)
+  cudaStream_t copy;        // copy-engine pushes and their signals
+  cudaEvent_t ev_in[FTM_SHARD_MAX_ROW_CHUNKS];
+  cudaEvent_t ev_owner[FTM_MAX_RANKS];
+  cudaEvent_t ev_pushed;    // last forward's a/b pushes done reading the local planes
+  cudaEvent_t ev_x_pushed;  // last forward's x pushes done reading the x blocks
+  int epoch;
+  int launches;             // kernels launched by the current forward
+  long long* trace;         // optional (time, tag) pairs of the current forward
+  int trace_n;
+};
+
+namespace {
+
+size_t elems_local(const ftm_shard_config* c) {
+  const size_t R = size_t(c->shard.rows), N = size_t(c->shard.cols);
+  return size_t(c->shard.batch) * kC * R * N;
+}
+
+int validate(const ftm_shard_config* c) {
+  if (!c) return FTM_BAD_ARGUMENT;
+  const ftm_problem& p = c->shard;
+  if (c->world < 1 || c->world > FTM_MAX_RANKS || c->rank < 0 || c->rank >= c->world)
+    return FTM_BAD_ARGUMENT;
+  if (c->scheme != FTM_SHARD_ALLTOALL && c->scheme != FTM_SHARD_ALLGATHER) return FTM_BAD_ARGUMENT;
+  if (c->scheme == FTM_SHARD_ALLGATHER && p.mode != FTM_OUTGOING) return FTM_BAD_ARGUMENT;
+  if (p.c_z != kC || p.c_h != kC || p.batch < 1 || p.rows < 1) return FTM_BAD_SHAPE;
+  if (p.cols != p.rows * c->world) return FTM_BAD_SHAPE;
+  if (c->row_chunks < 1 || c->row_chunks > FTM_SHARD_MAX_ROW_CHUNKS) return FTM_BAD_ARGUMENT;
+  if (p.batch > 1 && c->row_chunks != 1) return FTM_BAD_ARGUMENT;   // z rows are batch-strided
+  if (p.rows % c->row_chunks != 0) return FTM_BAD_SHAPE;
+  const int rc = p.rows / c->row_chunks;
+  if (rc % 128 != 0) return FTM_BAD_SHAPE;   // row / k blocks of the contraction
+  if (kC % c->world != 0 || (kC / c->world) % 8 != 0) return FTM_BAD_SHAPE;
+  if (p.mode != FTM_OUTGOING && p.mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
+  return FTM_OK;
+}
+
+int fail(cudaError_t e) { return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED; }
+
+// trace tags: (what << 8) | index
+enum { T_START = 1, T_INPUT = 2, T_AB_SENT = 3, T_AB_READY = 4, T_CONTRACT = 5, T_X_SENT = 6,
+       T_X_READY = 7, T_OUTPUT = 8 };
+void mark(ftm_shard_plan* pl, cudaStream_t s, int what, int index) {
+  if (!pl->trace || pl->trace_n >= FTM_SHARD_TRACE_POINTS) return;
+  mark_kernel<<<1, 1, 0, s>>>(pl->trace, pl->trace_n++, (what << 8) | index);
+}
+
+int wait_flags(ftm_shard_plan* pl, const FlagList& fl, int kind, cudaStream_t s) {
+  wait_flags_kernel<<<1, 32, 0, s>>>(pl->cfg.flags[pl->me], fl, pl->epoch, pl->cfg.err_word,
+                                     (KERNEL_EXCHANGE << 8) | (kind << 4) | 1);
+  ++pl->launches;
+  return fail(cudaGetLastError());
+}
+
+int signal(ftm_shard_plan* pl, int q, int word) {
+  signal_kernel<<<1, 1, 0, pl->copy>>>(pl->cfg.flags[q] + word, pl->epoch);
+  ++pl->launches;
+  return fail(cudaGetLastError());
+}
+
+// B rows of `width` bytes (1 row when B == 1): a plain peer copy or a 2-D one
+int copy_rows(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, int rows,
+              cudaStream_t s) {
+  if (rows == 1) return fail(cudaMemcpyAsync(dst, src, width, cudaMemcpyDefault, s));
+  return fail(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, cudaMemcpyDefault, s));
+}
+
+typedef unsigned short h16;   // fp16 element, for pointer arithmetic
+
+int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void* out,
+                     cudaStream_t cs) {
+  const ftm_shard_config& c = pl->cfg;
+  const int P = pl->P, me = pl->me, RC = pl->RC, rc = pl->rc, R = pl->R, N = pl->N, B = pl->B;
+  const int lq = pl->lq, L = pl->L;
+  const bool incoming = c.shard.mode == FTM_INCOMING;
+  const size_t unit = pl->unit;                                  // rc * N
+  const size_t blk = size_t(B) * lq * unit;                      // one (src, chunk) block
+  const size_t slot_elems = elems_local(&c);                     // one receive slot
+  const int slot = pl->epoch & 1;
+  int st;
+  // the previous forward's pushes must be done reading the local planes
+  if ((st = fail(cudaStreamWaitEvent(cs, pl->ev_pushed, 0))) != FTM_OK) return st;
+  mark(pl, cs, T_START, 0);
+  for (int r = 0; r < RC; ++r) {
+    ftm_problem sub = c.shard;
+    sub.rows = rc;
+    const size_t chunk = size_t(r) * L * unit;
+    h16* a_r = static_cast<h16*>(c.a_local) + chunk;
+    h16* b_r = static_cast<h16*>(c.b_local) + chunk;
+    const h16* z_r = static_cast<const h16*>(z) + size_t(r) * rc * N * kC;
+    const float* m_r = mask ? mask + size_t(r) * rc * N : nullptr;
+    if ((st = ftm_input_stage(&sub, z_r, m_r, c.packed, a_r, b_r, c.zstats + size_t(r) * rc * N * 2,
+                              c.err_word, cs)) != FTM_OK)
+      return st;
+    ++pl->launches;
+    mark(pl, cs, T_INPUT, r);
+    if ((st = fail(cudaEventRecord(pl->ev_in[r], cs))) != FTM_OK) return st;
+    if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_in[r], 0))) != FTM_OK) return st;
+    // shifted order: at any moment every rank sends to a different peer
+    for (int sft = 1; sft <= P; ++sft) {
+      const int q = (me + sft) % P;
+      const size_t off = size_t(slot) * slot_elems + size_t(me * RC + r) * blk;
+      const size_t src_off = size_t(q) * lq * unit;              // q's channels, batch 0
+      for (int ab = 0; ab < 2; ++ab) {
+        const h16* src = (ab ? b_r : a_r) + src_off;
+        h16* dst = static_cast<h16*>(ab ? c.recv_b[q] : c.recv_a[q]) + off;
+        if ((st = copy_rows(dst, size_t(lq) * unit * 2, src, size_t(kC) * unit * 2,
+                            size_t(lq) * unit * 2, B, pl->copy)) != FTM_OK)
+          return st;
+      }
+      if ((st = signal(pl, q, kFlagAB + me * FTM_SHARD_MAX_ROW_CHUNKS + r)) != FTM_OK) return st;
+      mark(pl, pl->copy, T_AB_SENT, q * 16 + r);
+    }
+  }
+  if ((st = fail(cudaEventRecord(pl->ev_pushed, pl->copy))) != FTM_OK) return st;
+
+  FlagList fl{};
+  for (int s = 0; s < P; ++s)
+    for (int r = 0; r < RC; ++r) fl.idx[fl.count++] = kFlagAB + s * FTM_SHARD_MAX_ROW_CHUNKS + r;
+  if ((st = wait_flags(pl, fl, 1, cs)) != FTM_OK) return st;
+  mark(pl, cs, T_AB_READY, 0);
+  // the previous forward's x pushes must be done reading the x blocks
+  if ((st = fail(cudaStreamWaitEvent(cs, pl->ev_x_pushed, 0))) != FTM_OK) return st;
+
+  const h16* Ra = static_cast<const h16*>(c.recv_a[me]) + size_t(slot) * slot_elems;
+  const h16* Rb = static_cast<const h16*>(c.recv_b[me]) + size_t(slot) * slot_elems;
+  const size_t owner_elems = size_t(B) * lq * R * N;
+  for (int sft = 1; sft <= P; ++sft) {
+    const int o = (me + sft) % P;
+    ftm_contraction_layout d{};
+    d.L = B * lq; d.m = R; d.n = N; d.k = N;
+    if (!incoming) {
+      // row blocks (src, chunk) of rc rows; owner o's rows are blocks [o*RC, (o+1)*RC)
+      d.k_per_block = N;
+      d.a = Ra + size_t(o) * RC * blk; d.a_rows_per_block = rc;
+      d.a_block_stride = blk; d.a_l_stride = unit; d.a_row_stride = N; d.a_kblock_stride = 0;
+      d.b = Rb; d.b_rows_per_block = rc;
+      d.b_block_stride = blk; d.b_l_stride = unit; d.b_row_stride = N; d.b_kblock_stride = 0;
+    } else {
+      // k blocks (src, chunk) of rc; planes [l][i][k in block]; owner o's rows i
+      d.k_per_block = rc;
+      d.a = Ra + size_t(o) * R * rc; d.a_rows_per_block = R;
+      d.a_block_stride = 0; d.a_l_stride = unit; d.a_row_stride = rc; d.a_kblock_stride = blk;
+      d.b = Rb; d.b_rows_per_block = N;
+      d.b_block_stride = 0; d.b_l_stride = unit; d.b_row_stride = rc; d.b_kblock_stride = blk;
+    }
+    const bool direct = (o == me && B == 1);
+    d.x = direct ? static_cast<void*>(static_cast<h16*>(c.x_plane[me]) + size_t(me) * lq * R * N)
+                 : static_cast<void*>(static_cast<h16*>(c.x_blocks) + size_t(o) * owner_elems);
+    d.x_rows_per_block = R; d.x_block_stride = 0; d.x_l_stride = size_t(R) * N; d.x_row_stride = N;
+    if ((st = ftm_contraction_general(&d, c.err_word, cs)) != FTM_OK) return st;
+    ++pl->launches;
+    mark(pl, cs, T_CONTRACT, o);
+    if (direct) continue;
+    if ((st = fail(cudaEventRecord(pl->ev_owner[o], cs))) != FTM_OK) return st;
+    if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_owner[o], 0))) != FTM_OK) return st;
+    h16* dst = static_cast<h16*>(c.x_plane[o]) + size_t(me) * lq * R * N;
+    if ((st = copy_rows(dst, size_t(kC) * R * N * 2, d.x, size_t(lq) * R * N * 2,
+                        size_t(lq) * R * N * 2, B, pl->copy)) != FTM_OK)
+      return st;
+    if ((st = signal(pl, o, kFlagX + me)) != FTM_OK) return st;
+    mark(pl, pl->copy, T_X_SENT, o);
+  }
+  if ((st = fail(cudaEventRecord(pl->ev_x_pushed, pl->copy))) != FTM_OK) return st;
+  FlagList fx{};
+  for (int s = 0; s < P; ++s)
+    if (s != me || B != 1) fx.idx[fx.count++] = kFlagX + s;
+  if (B != 1) {
+    // this rank's own x block still sits in the x blocks: copy it into the plane
+    h16* dst = static_cast<h16*>(c.x_plane[me]) + size_t(me) * lq * R * N;
+    const h16* src = static_cast<const h16*>(c.x_blocks) + size_t(me) * owner_elems;
+    if ((st = copy_rows(dst, size_t(kC) * R * N * 2, src, size_t(lq) * R * N * 2,
+                        size_t(lq) * R * N * 2, B, cs)) != FTM_OK)
+      return st;
+    fx.count = 0;
+    for (int s = 0; s < P; ++s)
+      if (s != me) fx.idx[fx.count++] = kFlagX + s;
+  }
+  if (fx.count && (st = wait_flags(pl, fx, 2, cs)) != FTM_OK) return st;
+  mark(pl, cs, T_X_READY, 0);
+  ++pl->launches;
+  st = ftm_output_stage(&c.shard, z, mask, c.x_plane[me], c.zstats, c.packed, out, c.err_word, cs);
+  mark(pl, cs, T_OUTPUT, 0);
+  return st;
+}
+
+int forward_allgather(ftm_shard_plan* pl, const void* z, const float* mask, void* out,
+                      cudaStream_t cs) {
+  const ftm_shard_config& c = pl->cfg;
+  const int P = pl->P, me = pl->me, RC = pl->RC, rc = pl->rc, R = pl->R, N = pl->N;
+  const int L = pl->L;
+  const size_t unit = pl->unit;
+  const size_t blk = size_t(L) * unit;                     // one (src, chunk) block of b
+  const size_t slot_elems = size_t(P) * RC * blk;
+  const int slot = pl->epoch & 1;
+  int st;
+  h16* own = static_cast<h16*>(c.recv_b[me]) + size_t(slot) * slot_elems;
+  if ((st = fail(cudaStreamWaitEvent(cs, pl->ev_pushed, 0))) != FTM_OK) return st;
+  mark(pl, cs, T_START, 0);
+  for (int r = 0; r < RC; ++r) {
+    ftm_problem sub = c.shard;
+    sub.rows = rc;
+    h16* a_r = static_cast<h16*>(c.a_local) + size_t(r) * blk;
+    h16* b_r = own + size_t(me * RC + r) * blk;             // b goes straight to its block
+    const h16* z_r = static_cast<const h16*>(z) + size_t(r) * rc * N * kC;
+    const float* m_r = mask ? mask + size_t(r) * rc * N : nullptr;
+    if ((st = ftm_input_stage(&sub, z_r, m_r, c.packed, a_r, b_r, c.zstats + size_t(r) * rc * N * 2,
+                              c.err_word, cs)) != FTM_OK)
+      return st;
+    ++pl->launches;
+    mark(pl, cs, T_INPUT, r);
+    if ((st = fail(cudaEventRecord(pl->ev_in[r], cs))) != FTM_OK) return st;
+    if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_in[r], 0))) != FTM_OK) return st;
+    for (int sft = 1; sft < P; ++sft) {
+      const int q = (me + sft) % P;
+      h16* dst = static_cast<h16*>(c.recv_b[q]) + size_t(slot) * slot_elems + size_t(me * RC + r) * blk;
+      if ((st = fail(cudaMemcpyAsync(dst, b_r, blk * 2, cudaMemcpyDefault, pl->copy))) != FTM_OK)
+        return st;
+      if ((st = signal(pl, q, kFlagAB + me * FTM_SHARD_MAX_ROW_CHUNKS + r)) != FTM_OK) return st;
+      mark(pl, pl->copy, T_AB_SENT, q * 16 + r);
+    }
+  }
+  if ((st = fail(cudaEventRecord(pl->ev_pushed, pl->copy))) != FTM_OK) return st;
+  // columns of source s, chunk r: B = that block (rc rows), X columns [s R + r rc, + rc)
+  auto contract = [&](int s, int r0, int nr) -> int {
+    ftm_contraction_layout d{};
+    d.L = L; d.m = R; d.n = nr * rc; d.k = N; d.k_per_block = N;
+    d.a = c.a_local; d.a_rows_per_block = rc;
+    d.a_block_stride = blk; d.a_l_stride = unit; d.a_row_stride = N;
+    d.b = own + size_t(s * RC + r0) * blk; d.b_rows_per_block = rc;
+    d.b_block_stride = blk; d.b_l_stride = unit; d.b_row_stride = N;
+    d.x = static_cast<h16*>(c.x_blocks) + size_t(s) * R + size_t(r0) * rc;
+    d.x_rows_per_block = R; d.x_l_stride = size_t(R) * N; d.x_row_stride = N;
+    ++pl->launches;
+    return ftm_contraction_general(&d, c.err_word, cs);
+  };
+  if ((st = contract(me, 0, RC)) != FTM_OK) return st;      // own b: no wait
+  mark(pl, cs, T_CONTRACT, me * 16);
+  for (int sft = 1; sft < P; ++sft) {
+    const int s = (me + P - sft) % P;                          // the order peers send to us
+    for (int r = 0; r < RC; ++r) {
+      FlagList fl{};
+      fl.idx[fl.count++] = kFlagAB + s * FTM_SHARD_MAX_ROW_CHUNKS + r;
+      if ((st = wait_flags(pl, fl, 1, cs)) != FTM_OK) return st;
+      mark(pl, cs, T_AB_READY, s * 16 + r);
+      if ((st = contract(s, r, 1)) != FTM_OK) return st;
+      mark(pl, cs, T_CONTRACT, s * 16 + r);
+    }
+  }
+  ++pl->launches;
+  st = ftm_output_stage(&c.shard, z, mask, c.x_blocks, c.zstats, c.packed, out, c.err_word, cs);
+  mark(pl, cs, T_OUTPUT, 0);
+  return st;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ftm_shard_buffer_bytes(const ftm_shard_config* cfg, int which) {
+  if (validate(cfg) != FTM_OK) return 0;
+  const size_t local = elems_local(cfg) * 2;
+  const size_t R = size_t(cfg->shard.rows), N = size_t(cfg->shard.cols), B = size_t(cfg->shard.batch);
+  switch (which) {
+    case FTM_SHARD_BUF_LOCAL: return local;
+    case FTM_SHARD_BUF_ZSTATS: return B * R * N * 8;
+    case FTM_SHARD_BUF_XBLOCKS: return local;
+    case FTM_SHARD_BUF_RECV:
+      return cfg->scheme == FTM_SHARD_ALLGATHER ? 2 * local * size_t(cfg->world) : 2 * local;
+    case FTM_SHARD_BUF_XPLANE: return local;
+    case FTM_SHARD_BUF_FLAGS: return FTM_SHARD_FLAG_WORDS * sizeof(int);
+    default: return 0;
+  }
+}
+
+int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
+  if (!plan) return FTM_BAD_ARGUMENT;
+  *plan = nullptr;
+  int st = validate(cfg);
+  if (st != FTM_OK) return st;
+  const bool a2a = cfg->scheme == FTM_SHARD_ALLTOALL;
+  if (!cfg->packed || !cfg->a_local || !cfg->zstats || !cfg->x_blocks || !cfg->err_word)
+    return FTM_BAD_ARGUMENT;
+  if (a2a && !cfg->b_local) return FTM_BAD_ARGUMENT;
+  for (int q = 0; q < cfg->world; ++q) {
+    if (!cfg->recv_b[q] || !cfg->flags[q]) return FTM_BAD_ARGUMENT;
+    if (a2a && (!cfg->recv_a[q] || !cfg->x_plane[q])) return FTM_BAD_ARGUMENT;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || ftm_device_supported(dev) != 1)
+    return FTM_UNSUPPORTED_ARCH;
+  ftm_shard_plan* pl = new (std::nothrow) ftm_shard_plan();
+  if (!pl) return FTM_LAUNCH_FAILED;
+  pl->cfg = *cfg;
+  pl->P = cfg->world;
+  pl->me = cfg->rank;
+  pl->RC = cfg->row_chunks;
+  pl->R = cfg->shard.rows;
+  pl->N = cfg->shard.cols;
+  pl->B = cfg->shard.batch;
+  pl->rc = pl->R / pl->RC;
+  pl->L = pl->B * kC;
+  pl->lq = kC / pl->P;
+  pl->unit = size_t(pl->rc) * pl->N;
+  pl->dev = dev;
+  pl->epoch = 0;
+  bool ok = cudaStreamCreateWithFlags(&pl->copy, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; ok && i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
+    ok = cudaEventCreateWithFlags(&pl->ev_in[i], cudaEventDisableTiming) == cudaSuccess;
+  for (int i = 0; ok && i < FTM_MAX_RANKS; ++i)
+    ok = cudaEventCreateWithFlags(&pl->ev_owner[i], cudaEventDisableTiming) == cudaSuccess;
+  ok = ok && cudaEventCreateWithFlags(&pl->ev_pushed, cudaEventDisableTiming) == cudaSuccess;
+  ok = ok && cudaEventCreateWithFlags(&pl->ev_x_pushed, cudaEventDisableTiming) == cudaSuccess;
+  // recorded once so the first forward's waits on them are satisfied
+  ok = ok && cudaEventRecord(pl->ev_pushed, pl->copy) == cudaSuccess;
+  ok = ok && cudaEventRecord(pl->ev_x_pushed, pl->copy) == cudaSuccess;
+  if (!ok) {
+    ftm_shard_plan_destroy(pl);
+    return FTM_LAUNCH_FAILED;
+  }
+  *plan = pl;
+  return FTM_OK;
+}
+
+int ftm_shard_forward(ftm_shard_plan* plan, const void* z, const float* mask, void* out,
+                      ftm_stream_t stream) {
+  set_last_launch_count(0);
+  if (!plan || !z || !out) return FTM_BAD_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(z) & 15u) || (reinterpret_cast<uintptr_t>(out) & 15u) ||
+      (reinterpret_cast<uintptr_t>(mask) & 15u))
+    return FTM_BAD_ALIGN;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != plan->dev) return FTM_BAD_ARGUMENT;
+  ++plan->epoch;
+  plan->launches = 0;
+  plan->trace_n = 0;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const int st = plan->cfg.scheme == FTM_SHARD_ALLTOALL ? forward_alltoall(plan, z, mask, out, cs)
+                                                         : forward_allgather(plan, z, mask, out, cs);
+  // the stage entry points set the per-thread count to 1 each; report the forward's total
+  set_last_launch_count(st == FTM_OK ? plan->launches : 0);
+  return st;
+}
+
+int ftm_shard_set_trace(ftm_shard_plan* plan, long long* trace) {
+  if (!plan) return FTM_BAD_ARGUMENT;
+  plan->trace = trace;
+  return FTM_OK;
+}
+
+void ftm_shard_plan_destroy(ftm_shard_plan* plan) {
+  if (!plan) return;
+  if (plan->copy) cudaStreamSynchronize(plan->copy);
+  for (int i = 0; i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
+    if (plan->ev_in[i]) cudaEventDestroy(plan->ev_in[i]);
+  for (int i = 0; i < FTM_MAX_RANKS; ++i)
+    if (plan->ev_owner[i]) cudaEventDestroy(plan->ev_owner[i]);
+  if (plan->ev_pushed) cudaEventDestroy(plan->ev_pushed);
+  if (plan->ev_x_pushed) cudaEventDestroy(plan->ev_x_pushed);
+  if (plan->copy) cudaStreamDestroy(plan->copy);
+  delete plan;
+}
+
+}  // extern "C"

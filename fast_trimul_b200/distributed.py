@@ -580,14 +580,300 @@ class RowShardedTriMul:
         comp.wait_stream(cs)
 
 
+# ------------------------------------------------------------- native pipeline
+PIPELINE_SCHEMES = ("p2p_alltoall", "p2p_allgather")
+
+
+def default_pipeline_scheme(world, mode="outgoing"):
+    """b all-gathered at 2 ranks (it sends (P-1)/P of one plane against 3(P-1)/P^2 for
+    the all-to-all, fewer at P = 2), the channel all-to-all from 4 ranks on and for
+    incoming mode."""
+    return "p2p_allgather" if world == 2 and mode == "outgoing" else "p2p_alltoall"
+
+
+def default_row_chunks(rows, batch=1):
+    """Row chunks of the input stage: each chunk's exchange starts when it is done.
+    Chunks of at least 128 rows (the contraction's row / k blocks), at most 4."""
+    if batch > 1:
+        return 1
+    for rc in (4, 3, 2):
+        if rows % rc == 0 and (rows // rc) % 128 == 0:
+            return rc
+    return 1
+
+
+class ShardedTriMul:
+    """Row-sharded forward on the library's native exchange pipeline (ftm_shard_forward).
+
+    Each rank of `group` owns rows [rank * N/P, (rank + 1) * N/P) of z and of the output.
+    One call queues this rank's whole forward on the current stream: the input stage in
+    row chunks, copy-engine pushes of each chunk into the peers' receive windows (CUDA IPC
+    mappings) with a flag raised in the receiver's memory after each push, bounded
+    device-side waits on those flags, the contraction and the output stage. NCCL is used
+    only here, at construction, to exchange the IPC handles. Every rank must make the
+    same calls in the same order.
+    """
+
+    def __init__(self, impl, batch, n, group=None, z_dtype=torch.bfloat16, out_dtype=None,
+                 device=None, scheme=None, row_chunks=None):
+        from ._module import device_error_word
+        import ctypes
+        self.impl, self.group = impl, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.batch, self.n = batch, n
+        lo, hi = row_range(n, self.world, self.rank)
+        self.rows = hi - lo
+        self.mode = impl.mode
+        scheme = scheme or default_pipeline_scheme(self.world, self.mode)
+        if scheme not in PIPELINE_SCHEMES:
+            raise ValueError(f"scheme must be one of {PIPELINE_SCHEMES}")
+        self.scheme = scheme
+        dev = torch.device(device) if device is not None else impl.proj_a.weight.device
+        self.device = dev
+        self.z_dtype = z_dtype
+        self.out_dtype = z_dtype if out_dtype is None else out_dtype
+        self.row_chunks = row_chunks or default_row_chunks(self.rows, batch)
+        lib = _lib.load()
+        self.lib = lib
+        probe = torch.empty(batch, self.rows, n, C, dtype=z_dtype, device="meta")
+        self.errw = device_error_word(dev)
+        self.packed = impl.packed_params()[0]
+        cfg = _lib.ShardConfig()
+        cfg.world, cfg.rank = self.world, self.rank
+        cfg.scheme = _lib.SHARD_ALLTOALL if scheme == "p2p_alltoall" else _lib.SHARD_ALLGATHER
+        cfg.row_chunks = self.row_chunks
+        cfg.shard = impl.problem(probe, self.out_dtype)
+        self._probs = {self.out_dtype: cfg.shard}
+
+        def nbytes(which):
+            v = lib.ftm_shard_buffer_bytes(ctypes.byref(cfg), which)
+            if v == 0:
+                raise ValueError(f"unsupported sharded problem: B={batch} N={n} P={self.world} "
+                                 f"row_chunks={self.row_chunks} scheme={scheme} mode={self.mode}")
+            return v
+
+        def buf(which):
+            return torch.empty(nbytes(which), dtype=torch.uint8, device=dev)
+
+        a2a = scheme == "p2p_alltoall"
+        self.a_local = buf(_lib.SHARD_BUF_LOCAL)
+        self.b_local = buf(_lib.SHARD_BUF_LOCAL) if a2a else None
+        self.zstats = buf(_lib.SHARD_BUF_ZSTATS)
+        self.x_blocks = buf(_lib.SHARD_BUF_XBLOCKS)
+        self.windows = {}
+        names = ("recv_a", "recv_b", "x_plane", "flags") if a2a else ("recv_b", "flags")
+        sizes = {"recv_a": _lib.SHARD_BUF_RECV, "recv_b": _lib.SHARD_BUF_RECV,
+                 "x_plane": _lib.SHARD_BUF_XPLANE, "flags": _lib.SHARD_BUF_FLAGS}
+        for name in names:
+            if self.world > 1:
+                w = PeerWindow(nbytes(sizes[name]), dev, group)
+            else:
+                w = _LocalWindow(nbytes(sizes[name]), dev)
+            self.windows[name] = w
+        self.windows["flags"].tensor.zero_()
+        torch.cuda.synchronize(dev)
+        cfg.packed = self.packed.data_ptr()
+        cfg.a_local = self.a_local.data_ptr()
+        cfg.b_local = self.b_local.data_ptr() if a2a else None
+        cfg.zstats = self.zstats.data_ptr()
+        cfg.x_blocks = self.x_blocks.data_ptr()
+        cfg.err_word = self.errw.ptr
+        for name, w in self.windows.items():
+            arr = getattr(cfg, name)
+            for q, p in enumerate(w.ptrs):
+                arr[q] = p
+        self.cfg = cfg
+        self.plan = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(lib.ftm_shard_plan_create(ctypes.byref(cfg), ctypes.byref(self.plan)),
+                       "ftm_shard_plan_create")
+        self._plans = {self.out_dtype: self.plan}
+        if self.world > 1:
+            dist.barrier(group=group)         # every rank's flags are zero before any push
+
+    def _plan_for(self, out_dtype):
+        """Plans differ only in the output dtype of the problem; one per dtype, sharing
+        every buffer (calls run in stream order, so they never overlap)."""
+        import ctypes
+        if out_dtype not in self._plans:
+            cfg = _lib.ShardConfig.from_buffer_copy(self.cfg)
+            probe = torch.empty(self.batch, self.rows, self.n, C, dtype=self.z_dtype, device="meta")
+            cfg.shard = self.impl.problem(probe, out_dtype)
+            plan = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(self.lib.ftm_shard_plan_create(ctypes.byref(cfg), ctypes.byref(plan)),
+                           "ftm_shard_plan_create")
+            self._plans[out_dtype] = plan
+        return self._plans[out_dtype]
+
+    def comm_bytes_per_step(self):
+        """Bytes this rank sends over NVLink per forward."""
+        plane = self.batch * C * self.rows * self.n * 2            # this rank's a (or b, or x)
+        P = self.world
+        if self.scheme == "p2p_allgather":
+            return (P - 1) * plane
+        return 3 * plane * (P - 1) // P
+
+    def __call__(self, z_local, mask_local=None, out=None):
+        shape = (self.batch, self.rows, self.n, C)
+        if tuple(z_local.shape) != shape or z_local.dtype != self.z_dtype or not z_local.is_contiguous():
+            raise ValueError(f"z_local must be a contiguous {self.z_dtype} tensor of shape {shape}")
+        if mask_local is not None:
+            mask_local = mask_local.to(device=self.device, dtype=torch.float32).expand(shape[:3]).contiguous()
+        if out is None:
+            out = torch.empty(shape, dtype=self.out_dtype, device=self.device)
+        self.errw.poll()
+        plan = self._plan_for(out.dtype)
+        st = self.lib.ftm_shard_forward(plan, z_local.data_ptr(),
+                                        None if mask_local is None else mask_local.data_ptr(),
+                                        out.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(st, "ftm_shard_forward")
+        self.last_launches = self.lib.ftm_last_launch_count()
+        self.errw.after_launch()
+        _lib.stats["calls"] += 1
+        _lib.stats["kernel_launches"] += self.last_launches
+        return out
+
+    def check(self):
+        self.errw.check()
+
+    TRACE_NAMES = {1: "start", 2: "input", 3: "pushed", 4: "ready", 5: "contracted", 6: "x_pushed",
+                   7: "x_ready", 8: "output"}
+
+    def enable_trace(self):
+        """Record a device-clock timeline of each later forward (ftm_shard_set_trace)."""
+        self._trace = torch.zeros(2 * 128, dtype=torch.int64, device=self.device)
+        for plan in self._plans.values():
+            _lib.check(self.lib.ftm_shard_set_trace(plan, self._trace.data_ptr()), "ftm_shard_set_trace")
+
+    def read_trace(self):
+        """[(microseconds since the forward's start, event, index)] of the last forward."""
+        torch.cuda.synchronize(self.device)
+        t = self._trace.view(-1, 2).cpu().tolist()
+        pts = [(ts, tag) for ts, tag in t if tag]
+        if not pts:
+            return []
+        t0 = min(ts for ts, tag in pts if tag >> 8 == 1)
+        return sorted((round((ts - t0) / 1e3, 1), self.TRACE_NAMES.get(tag >> 8, str(tag >> 8)),
+                       tag & 255) for ts, tag in pts)
+
+    def close(self):
+        """Destroy the plans and unmap the peers' windows; call on every rank after the
+        last forward, before the process group is destroyed."""
+        torch.cuda.synchronize(self.device)
+        for plan in self._plans.values():
+            self.lib.ftm_shard_plan_destroy(plan)
+        self._plans = {}
+        for w in self.windows.values():
+            w.close()
+
+
+class _LocalWindow:
+    """One rank: a plain device buffer in place of a peer window."""
+
+    def __init__(self, nbytes, device):
+        self.tensor = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self.ptrs = [self.tensor.data_ptr()]
+
+    def close(self):
+        pass
+
+
 # --------------------------------------------------------------------------- bench
 def _flops(n, batch=1):
     m = batch * n * n
     return 12 * m * C * C + 2 * batch * C * n ** 3
 
 
+def _sharded_parity(impl, z, mask, out_f32, group, rows_total=16):
+    """Checks this rank's fp32 output rows against the fp32 formula of the reference's
+    torch path (fast_trimul_b200.parity) on rows spread over ALL ranks' rows: z is
+    all-gathered so every rank can form b over all rows. Returns, on every rank, the
+    max-abs and mean-relative error over the rows every rank checked."""
+    from .parity import reference_rows, sample_rows
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, R, N, _ = z.shape
+    parts = [torch.empty_like(z) for _ in range(world)]
+    dist.all_gather(parts, z.contiguous(), group=group)
+    zf = torch.cat(parts, dim=1)
+    mf = None
+    if mask is not None:
+        mparts = [torch.empty_like(mask) for _ in range(world)]
+        dist.all_gather(mparts, mask.contiguous(), group=group)
+        mf = torch.cat(mparts, dim=1)
+    per = max(2, rows_total // world)
+    local = sample_rows(R, per)
+    ref = reference_rows(impl, zf, mf, [rank * R + i for i in local])
+    got = out_f32[:, local].double()
+    d = (got - ref.double()).abs()
+    stats = torch.tensor([d.max().item(), d.sum().item(), ref.double().abs().sum().item(),
+                          float(len(local))], device=z.device, dtype=torch.float64)
+    mx = stats[:1].clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(stats, group=group)
+    max_abs, mean_rel = mx.item(), stats[1].item() / stats[2].item()
+    del zf, parts
+    return {"max_abs": round(max_abs, 6), "mean_rel": round(mean_rel, 7),
+            "rows_checked": int(stats[3].item()), "ranks": world,
+            "tolerance": {"max_abs": 2e-2, "mean_rel": 1e-3},
+            "ok": bool(max_abs <= 2e-2 and mean_rel <= 1e-3),
+            "checker": "fp32 torch formula of the reference's torch path on the all-gathered z, "
+                       "rows sampled on every rank",
+            "output": "fp32 (same sharded forward; the timed steps write bf16)"}
+
+
+def _stages_alone(impl, n, world, dev, reps=10):
+    """CUDA-event time of each of one rank's kernels run alone on local data (no
+    exchange): the input stage on N/P rows, the contraction of this rank's share
+    (128/P channels over all rows -- C R N^2 multiply-adds either way) and the output stage
+    on N/P rows. The roofline of the sharded run is quoted on these."""
+    lib = _lib.load()
+    R = n // world
+    s = torch.cuda.current_stream().cuda_stream
+    z = torch.randn(1, R, n, C, device=dev).to(torch.bfloat16)
+    mask = torch.ones(1, R, n, device=dev)
+    plane = C * R * n
+    a = torch.empty(plane, dtype=torch.float16, device=dev)
+    b = torch.empty_like(a)
+    x = torch.randn(plane, device=dev).half()
+    A = torch.randn(C // world, n, n, device=dev).half()
+    Bm = torch.randn(C // world, n, n, device=dev).half()
+    X = torch.empty_like(A)
+    out = torch.empty_like(z)
+    zst = torch.empty(R * n * 2, dtype=torch.float32, device=dev)
+    err = torch.zeros(64, dtype=torch.int32, device=dev)
+    packed = impl.packed_params()[0]
+    prob = impl.problem(z, torch.bfloat16)
+    calls = {
+        "input_stage": lambda: lib.ftm_input_stage(prob, z.data_ptr(), mask.data_ptr(), packed.data_ptr(),
+                                                   a.data_ptr(), b.data_ptr(), zst.data_ptr(),
+                                                   err.data_ptr(), s),
+        "contraction": lambda: lib.ftm_contraction(A.data_ptr(), Bm.data_ptr(), X.data_ptr(), C // world,
+                                                   n, n, n, 1, err.data_ptr(), s),
+        "output_stage": lambda: lib.ftm_output_stage(prob, z.data_ptr(), mask.data_ptr(), x.data_ptr(),
+                                                     zst.data_ptr(), packed.data_ptr(), out.data_ptr(),
+                                                     err.data_ptr(), s),
+    }
+    res = {}
+    for name, f in calls.items():
+        for _ in range(3):
+            _lib.check(f(), name)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+        ev[0].record()
+        for i in range(reps):
+            f()
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        res[name] = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(reps))[reps // 2]
+    if lib.ftm_check_error(err.data_ptr(), None, s) != _lib.OK:
+        raise _lib.NativeKernelError("a stage timed alone reported an expired wait")
+    return res
+
+
 def bench_sharded(args, torch_mod):
-    """bench.py's multi-GPU arm: one N x N outgoing TriMul, rows sharded over ranks.
+    """bench.py's multi-GPU arm: one N x N TriMul, rows sharded over ranks.
     Returns the timing dict on rank 0, None elsewhere."""
     from fast_trimul_b200 import FastTriangleMultiplication
     rank = int(os.environ.get("RANK", "0"))
@@ -605,45 +891,70 @@ def bench_sharded(args, torch_mod):
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     z = torch.randn(1, hi - lo, n, C, device=dev, generator=gen).to(torch.bfloat16)
     mask = torch.ones(1, hi - lo, n, device=dev)
-    scheme = getattr(args, "scheme", None) or default_scheme(world, mode)
-    chunks = getattr(args, "chunks", None) or (4 if scheme.startswith("allgather") else 2)
-    sh = RowShardedTriMul(layer._impl, 1, n, chunks=chunks, device=dev, scheme=scheme)
+    scheme = getattr(args, "scheme", None) or default_pipeline_scheme(world, mode)
+    if scheme in PIPELINE_SCHEMES:
+        sh = ShardedTriMul(layer._impl, 1, n, device=dev, scheme=scheme,
+                           row_chunks=getattr(args, "row_chunks", None))
+        run = sh
+        check = sh.check
+        detail = {"scheme": scheme, "row_chunks": sh.row_chunks}
+    else:
+        chunks = getattr(args, "chunks", None) or (4 if scheme.startswith("allgather") else 2)
+        sh = RowShardedTriMul(layer._impl, 1, n, chunks=chunks, device=dev, scheme=scheme)
+        run = sh
+        check = sh.ops.check
+        detail = {"scheme": scheme, "chunks": chunks}
     out = torch.empty_like(z)
     for _ in range(args.warmup):
-        sh(z, mask, out=out)
-    sh.ops.check()
+        run(z, mask, out=out)
+    check()
     K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     from bench import ClockSampler
     dist.barrier()
     torch.cuda.synchronize()
+    n_launch0 = _lib.stats["kernel_launches"]
     with ClockSampler(local) as clk:
         t0.record()
         for k in range(K):
-            sh(z, mask, out=out, events=evs[k])
+            run(z, mask, out=out)
         t1.record()
         torch.cuda.synchronize()
+    launches = _lib.stats["kernel_launches"] - n_launch0
     dist.barrier()
-    sh.ops.check()
+    check()
+    trace = None
+    if getattr(args, "trace", False) and hasattr(sh, "enable_trace"):
+        sh.enable_trace()
+        for _ in range(3):
+            run(z, mask, out=out)
+        mine = sh.read_trace()
+        allt = [None] * world
+        dist.all_gather_object(allt, mine)
+        trace = allt
+        for plan in sh._plans.values():
+            sh.lib.ftm_shard_set_trace(plan, None)
     ms = torch.tensor([t0.elapsed_time(t1) / K], device=dev)
-    st = torch.tensor([sum(e[0].elapsed_time(e[1]) for e in evs) / K,
-                       sum(e[1].elapsed_time(e[2]) for e in evs) / K,
-                       sum(e[2].elapsed_time(e[3]) for e in evs) / K], device=dev)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    dist.all_reduce(st, op=dist.ReduceOp.MAX)
     clocks = clk.summary()
+    # parity of the same sharded forward (fp32 output) on rows of every rank
+    out32 = torch.empty(z.shape, dtype=torch.float32, device=dev)
+    run(z, mask, out=out32)
+    check()
+    parity = _sharded_parity(layer._impl, z, mask, out32, None)
+    del out32
     # end to end through the same public object: this rank's z rows from pinned host
     # memory in, its output rows back out, inside the timed region
     z_host = z.cpu().pin_memory()
     m_host = mask.cpu().pin_memory()
     o_host = torch.empty_like(z_host).pin_memory()
     e2e_steps = max(3, min(K, 20))
+    zd, md = torch.empty_like(z), torch.empty_like(mask)
 
     def e2e_step():
-        zd = z_host.to(dev, non_blocking=True)
-        md = m_host.to(dev, non_blocking=True)
-        o_host.copy_(sh(zd, md), non_blocking=True)
+        zd.copy_(z_host, non_blocking=True)
+        md.copy_(m_host, non_blocking=True)
+        o_host.copy_(run(zd, md, out=out), non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -657,21 +968,27 @@ def bench_sharded(args, torch_mod):
     torch.cuda.synchronize()
     e2e_ms = torch.tensor([a0.elapsed_time(a1) / e2e_steps], device=dev)
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    check()
+    stage_ms = _stages_alone(layer._impl, n, world, dev)
     res = None
     if rank == 0:
+        detail.update({"bytes_sent_per_rank_per_step": sh.comm_bytes_per_step(),
+                       "nvlink_gbs_per_rank": round(sh.comm_bytes_per_step() / (ms.item() * 1e-3) / 1e9, 1)})
         res = {"ms_per_step": ms.item(), "rows_per_rank": hi - lo,
-               "stage_ms": {"input_stage": st[0].item(), "contraction": st[1].item(),
-                            "output_stage": st[2].item()},
-               "clocks": clocks, "gpu_launches": (2 + sh.chunks) * K,
-               "comm": {"bytes_recv_per_rank_per_step": sh.comm_bytes_per_step(),
-                        "chunks": sh.chunks, "scheme": sh.scheme,
-                        "note": "contraction stage time includes the chunked exchange it waits on"},
+               "clocks": clocks, "gpu_launches": launches, "parity": parity,
+               "trace": trace,
+               "stage_ms": stage_ms, "stage_note": "each kernel of one rank timed alone on local "
+                                                   "data; the step adds the exchange",
+               "comm": detail,
                "e2e": {"value": round(_flops(n) / (e2e_ms.item() * 1e-3) / 1e12, 3),
                        "unit": "TFLOP/s", "ms_per_step": round(e2e_ms.item(), 3),
                        "steps": e2e_steps,
                        "h2d_bytes_per_step": world * (z_host.numel() * 2 + m_host.numel() * 4),
                        "d2h_bytes_per_step": world * o_host.numel() * 2},
                "sweep": None}
+    dist.barrier()
+    if hasattr(sh, "close"):
+        sh.close()
     dist.barrier()
     dist.destroy_process_group()
     return res

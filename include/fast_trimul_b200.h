@@ -102,7 +102,7 @@ int ftm_input_stage(const ftm_problem* p, const void* z, const float* mask, cons
  * per-rank row shards produces), so B row j lives in block j / b_rows_per_block.
  * X is (L, m, n) with n = b_blocks * b_rows_per_block. Replaces outgoing()/incoming()
  * (_kernels.py:131-162). Requires k % 8 == 0 and, when b_blocks > 1,
- * b_rows_per_block % 256 == 0. */
+ * b_rows_per_block % 128 == 0. */
 int ftm_contraction(const void* A, const void* B, void* X, int32_t L, int32_t m, int32_t k,
                     int32_t b_rows_per_block, int32_t b_blocks, int* err_word,
                     ftm_stream_t stream);
@@ -129,6 +129,38 @@ int ftm_contraction_blocked(const void* A, const void* B, void* X, int32_t L,
 int ftm_contraction_kblocked(const void* A, const void* B, void* X, int32_t L, int32_t m,
                              int32_t n, int32_t k_rows_per_block, int32_t k_blocks,
                              int32_t x_rows_per_block, int* err_word, ftm_stream_t stream);
+
+/* General strided contraction -- the form the sharded forward uses for its partial
+ * problems (one row owner's block, one source's columns, received channel shards):
+ *   X[l][i][j] = sum_kk A[l][i][kk] * B[l][j][kk],  l < L, i < m, j < n, kk < k,
+ * fp16 operands, fp32 accumulation, fp16 X, on the CTA-pair tensor-core kernel. Every
+ * operand is described by element strides:
+ *   A[l][i][kk] = a[(i / a_rows_per_block) * a_block_stride + l * a_l_stride
+ *                   + (i % a_rows_per_block) * a_row_stride
+ *                   + (kk / k_per_block) * a_kblock_stride + kk % k_per_block]
+ *   B[l][j][kk] likewise with j and the b_* fields,
+ *   X[l][i][j]  = x[(i / x_rows_per_block) * x_block_stride + l * x_l_stride
+ *                   + (i % x_rows_per_block) * x_row_stride + j].
+ * A rows-per-block or k_per_block of 0 (or >= the extent) means one block. Rules: 16-byte
+ * aligned pointers; strides multiples of 8 elements (block strides may be 0 when there is
+ * one block); n % 8 == 0; several row blocks need rows_per_block % 128 == 0 and the extent
+ * a multiple of it; several k blocks need k_per_block % 64 == 0 and k a multiple of it.
+ * Same reference code as ftm_contraction (_kernels.py:131-162). */
+typedef struct {
+  int32_t L, m, n, k;
+  int32_t k_per_block;
+  const void* a;
+  int32_t a_rows_per_block;
+  int64_t a_block_stride, a_l_stride, a_row_stride, a_kblock_stride;
+  const void* b;
+  int32_t b_rows_per_block;
+  int64_t b_block_stride, b_l_stride, b_row_stride, b_kblock_stride;
+  void* x;
+  int32_t x_rows_per_block;
+  int64_t x_block_stride, x_l_stride, x_row_stride;
+} ftm_contraction_layout;
+int ftm_contraction_general(const ftm_contraction_layout* layout, int* err_word,
+                            ftm_stream_t stream);
 
 /* Output stage: LayerNorm over c_h of x (channel-major fp16), the c_h -> c_z projection,
  * sigmoid(z_n W_g + b_g) gate, residual and mask, stored in out_dtype. Replaces
@@ -175,6 +207,66 @@ int ftm_input_stage_scatter(const ftm_problem* p, const void* z, const float* ma
 int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes* x_dst,
                             int32_t batch, int32_t c_h, int32_t rows, int32_t n, int32_t mode,
                             int* err_word, ftm_stream_t stream);
+
+/* ---- row-sharded multi-GPU forward, native exchange pipeline ----------------
+ * No counterpart in the reference (it has no multi-GPU path). P ranks, one GPU each,
+ * rank r owning R = N / P consecutive rows of z and of the output. One call runs the
+ * whole sharded forward of this rank on `stream`: the input stage in row_chunks
+ * launches; copy-engine pushes of each chunk's pieces into the peers' receive windows
+ * (CUDA IPC mappings) as soon as it is done, each followed by a flag raised in the
+ * receiver's memory; bounded device-side waits on those flags; the contraction
+ * (alltoall: this rank's channels for one row owner at a time, each owner's x block
+ * pushed back as soon as it is done; allgather: own rows against each arriving chunk of
+ * b); the output stage. No NCCL call and no host synchronisation on the data path.
+ * Every rank must call ftm_shard_forward the same number of times; an expired wait is
+ * reported through err_word (ftm_check_error), never by hanging.
+ * Buffer sizes come from ftm_shard_buffer_bytes; recv_*, x_plane and flags are per rank
+ * as mapped in this process (this rank's own entry is its local buffer); flags must be
+ * zeroed before the first forward. The plan owns one copy stream and a few events (no
+ * device memory). Requirements: rows % row_chunks == 0, rows / row_chunks % 128 == 0,
+ * (128 / P) % 8 == 0, row_chunks == 1 when batch > 1. */
+#define FTM_SHARD_ALLTOALL 0
+#define FTM_SHARD_ALLGATHER 1
+#define FTM_SHARD_MAX_ROW_CHUNKS 8
+#define FTM_SHARD_FLAG_WORDS 256
+enum {
+  FTM_SHARD_BUF_LOCAL = 0,   /* a_local, b_local: this rank's projections, chunk-major */
+  FTM_SHARD_BUF_ZSTATS = 1,  /* zstats */
+  FTM_SHARD_BUF_XBLOCKS = 2, /* x_blocks: alltoall -- x per row owner; allgather -- x plane */
+  FTM_SHARD_BUF_RECV = 3,    /* each receive window (two slots) */
+  FTM_SHARD_BUF_XPLANE = 4,  /* each x plane (alltoall) */
+  FTM_SHARD_BUF_FLAGS = 5    /* each flag buffer */
+};
+typedef struct {
+  int32_t world, rank;
+  int32_t scheme;       /* FTM_SHARD_ALLTOALL (both modes) or FTM_SHARD_ALLGATHER (outgoing) */
+  int32_t row_chunks;   /* 1..FTM_SHARD_MAX_ROW_CHUNKS */
+  ftm_problem shard;    /* this rank's rows: rows = N / world, cols = N */
+  const void* packed;
+  void* a_local;
+  void* b_local;        /* alltoall only */
+  float* zstats;
+  void* x_blocks;
+  int* err_word;
+  void* recv_a[FTM_MAX_RANKS];   /* alltoall only */
+  void* recv_b[FTM_MAX_RANKS];
+  void* x_plane[FTM_MAX_RANKS];  /* alltoall only */
+  int* flags[FTM_MAX_RANKS];
+} ftm_shard_config;
+typedef struct ftm_shard_plan ftm_shard_plan;
+size_t ftm_shard_buffer_bytes(const ftm_shard_config* cfg, int which);
+int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan);
+int ftm_shard_forward(ftm_shard_plan* plan, const void* z, const float* mask, void* out,
+                      ftm_stream_t stream);
+void ftm_shard_plan_destroy(ftm_shard_plan* plan);
+/* Optional timeline of the following forwards (for profiling): `trace` is a device buffer
+ * of 2 * FTM_SHARD_TRACE_POINTS int64; each forward overwrites it with (device clock ns,
+ * tag) pairs taken when the work queued before each point has finished -- tag =
+ * (what << 8) | index, what: 1 start, 2 input chunk done, 3 chunk pushed to a peer,
+ * 4 data ready, 5 contraction done, 6 x pushed, 7 x ready, 8 output done. The extra
+ * one-thread kernels cost a few microseconds each. NULL turns it off. */
+#define FTM_SHARD_TRACE_POINTS 128
+int ftm_shard_set_trace(ftm_shard_plan* plan, long long* trace);
 
 /* ---- whole forward with no allocation ---------------------------------------
  * No counterpart in the reference. For callers that cannot provide a workspace --

@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, path, scheme, mode="outgoing"):
+def _worker(rank, world, port, path, scheme, mode="outgoing", row_chunks=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -38,10 +38,22 @@ def _worker(rank, world, port, path, scheme, mode="outgoing"):
         mask = torch.ones(1, N, N)
         mask[:, :, N - 40:] = 0
         lo, hi = row_range(N, world, rank)
-        sh = RowShardedTriMul(m._impl, 1, N, chunks=4, device=dev, out_dtype=torch.float32,
-                              scheme=scheme)
-        out = sh(z[:, lo:hi].contiguous().to(dev), mask[:, lo:hi].contiguous().to(dev))
-        sh.ops.check()
+        zl = z[:, lo:hi].contiguous().to(dev)
+        ml = mask[:, lo:hi].contiguous().to(dev)
+        if scheme.startswith("p2p_"):
+            from fast_trimul_b200.distributed import ShardedTriMul
+            sh = ShardedTriMul(m._impl, 1, N, device=dev, out_dtype=torch.float32, scheme=scheme,
+                               row_chunks=row_chunks)
+            # three forwards in a row: the receive windows alternate, flags count epochs
+            for _ in range(3):
+                out = sh(zl, ml)
+            sh.check()
+            sh.close()
+        else:
+            sh = RowShardedTriMul(m._impl, 1, N, chunks=4, device=dev, out_dtype=torch.float32,
+                                  scheme=scheme)
+            out = sh(zl, ml)
+            sh.ops.check()
         parts = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(parts, out)
         if rank == 0:
@@ -51,7 +63,9 @@ def _worker(rank, world, port, path, scheme, mode="outgoing"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("scheme,mode", [("allgather", "outgoing"), ("alltoall", "outgoing"),
+@pytest.mark.parametrize("scheme,mode", [("p2p_allgather", "outgoing"), ("p2p_alltoall", "outgoing"),
+                                         ("p2p_alltoall", "incoming"),
+                                         ("allgather", "outgoing"), ("alltoall", "outgoing"),
                                          ("allgather_ce", "outgoing"), ("alltoall_ce", "outgoing"),
                                          ("fused", "outgoing"), ("alltoall_ce", "incoming"),
                                          ("fused", "incoming")])
@@ -82,3 +96,31 @@ def test_single_rank_sharded_object_matches_plain_forward():
     with torch.no_grad():
         want = m._impl._forward_native(z, None, out_dtype=torch.float32)
     assert torch.equal(got, want)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
+@pytest.mark.parametrize("scheme,mode,row_chunks", [("p2p_alltoall", "outgoing", 2),
+                                                    ("p2p_alltoall", "incoming", 2),
+                                                    ("p2p_allgather", "outgoing", 2),
+                                                    ("p2p_alltoall", "outgoing", 1)])
+def test_single_rank_native_pipeline(scheme, mode, row_chunks):
+    """world = 1: the native pipeline (row-chunked input stage, copies into its own
+    receive window, flag waits, strided contractions) equals the plain forward, over
+    several forwards (alternating receive slots, increasing flag epochs)."""
+    from fast_trimul_b200.distributed import ShardedTriMul
+    from tests.helpers import make_layer
+    m = make_layer(mode, True).cuda()
+    g = torch.Generator(device="cuda").manual_seed(22)
+    sh = ShardedTriMul(m._impl, 1, 256, device="cuda", out_dtype=torch.float32, scheme=scheme,
+                       row_chunks=row_chunks)
+    for it in range(3):
+        z = torch.randn(1, 256, 256, 128, device="cuda", generator=g).to(torch.bfloat16)
+        mask = torch.ones(1, 256, 256, device="cuda")
+        mask[:, :, 250:] = 0
+        got = sh(z, mask)
+        with torch.no_grad():
+            want = m._impl._forward_native(z, mask, out_dtype=torch.float32)
+        sh.check()
+        d = (got - want).abs().max().item()
+        assert d <= 2e-3, (it, d)
+    sh.close()

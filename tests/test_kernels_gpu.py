@@ -235,6 +235,70 @@ def test_contraction_kblocked(kernel, monkeypatch):
 
 
 @needs_gpu
+@pytest.mark.parametrize("case", ["row_blocks_padded", "k_blocks_row_offset", "x_column_window"])
+def test_contraction_general_strided(case):
+    """ftm_contraction_general on the partial problems the sharded pipeline issues:
+    A / B in 128-row blocks with padded row strides, k split into 128-wide blocks with
+    A starting at a row offset inside each block, and X written into a column window of
+    a wider matrix -- against an fp32 matmul of the same operands."""
+    import ctypes
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(13)
+    s = torch.cuda.current_stream().cuda_stream
+    err = torch.zeros(64, dtype=torch.int32, device="cuda")
+    d = _lib.ContractionLayout()
+    L = 3
+    if case == "row_blocks_padded":
+        m, n, k, rpb, pad = 256, 384, 200, 128, 8
+        Ab = torch.randn(m // rpb, L, rpb, k + pad, device="cuda", generator=g).half()
+        Bb = torch.randn(n // rpb, L, rpb, k + pad, device="cuda", generator=g).half()
+        A = Ab[..., :k].permute(1, 0, 2, 3).reshape(L, m, k)
+        B = Bb[..., :k].permute(1, 0, 2, 3).reshape(L, n, k)
+        X = torch.full((L, m, n), float("nan"), device="cuda", dtype=torch.half)
+        d.L, d.m, d.n, d.k, d.k_per_block = L, m, n, k, 0
+        d.a, d.a_rows_per_block = Ab.data_ptr(), rpb
+        d.a_block_stride, d.a_l_stride, d.a_row_stride = L * rpb * (k + pad), rpb * (k + pad), k + pad
+        d.b, d.b_rows_per_block = Bb.data_ptr(), rpb
+        d.b_block_stride, d.b_l_stride, d.b_row_stride = L * rpb * (k + pad), rpb * (k + pad), k + pad
+        d.x, d.x_rows_per_block, d.x_l_stride, d.x_row_stride = X.data_ptr(), 0, m * n, n
+        got = X
+    elif case == "k_blocks_row_offset":
+        kb, nkb, rows_all, off, m = 128, 3, 512, 256, 256
+        Ab = torch.randn(nkb, L, rows_all, kb, device="cuda", generator=g).half()
+        Bb = torch.randn(nkb, L, rows_all, kb, device="cuda", generator=g).half()
+        A = Ab[:, :, off:off + m].permute(1, 2, 0, 3).reshape(L, m, nkb * kb)
+        B = Bb.permute(1, 2, 0, 3).reshape(L, rows_all, nkb * kb)
+        X = torch.full((L, m, rows_all), float("nan"), device="cuda", dtype=torch.half)
+        d.L, d.m, d.n, d.k, d.k_per_block = L, m, rows_all, nkb * kb, kb
+        d.a, d.a_rows_per_block = Ab.data_ptr() + off * kb * 2, 0
+        d.a_l_stride, d.a_row_stride, d.a_kblock_stride = rows_all * kb, kb, L * rows_all * kb
+        d.b, d.b_rows_per_block = Bb.data_ptr(), 0
+        d.b_l_stride, d.b_row_stride, d.b_kblock_stride = rows_all * kb, kb, L * rows_all * kb
+        d.x, d.x_l_stride, d.x_row_stride = X.data_ptr(), m * rows_all, rows_all
+        got = X
+    else:
+        m, n, k, wide, col0 = 128, 256, 256, 768, 256
+        A = torch.randn(L, m, k, device="cuda", generator=g).half()
+        B = torch.randn(L, n, k, device="cuda", generator=g).half()
+        Xw = torch.full((L, m, wide), 5.0, device="cuda", dtype=torch.half)
+        d.L, d.m, d.n, d.k, d.k_per_block = L, m, n, k, 0
+        d.a, d.a_l_stride, d.a_row_stride = A.data_ptr(), m * k, k
+        d.b, d.b_l_stride, d.b_row_stride = B.data_ptr(), n * k, k
+        d.x, d.x_l_stride, d.x_row_stride = Xw.data_ptr() + col0 * 2, m * wide, wide
+        got = Xw[:, :, col0:col0 + n]
+    st = lib.ftm_contraction_general(ctypes.byref(d), err.data_ptr(), s)
+    assert st == 0, _lib.status_string(st)
+    assert lib.ftm_check_error(err.data_ptr(), None, s) == 0
+    ref = torch.bmm(A.float(), B.float().transpose(1, 2))
+    assert torch.isfinite(got).all()
+    rel = ((got.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 2e-3, rel
+    if case == "x_column_window":        # nothing outside the window was written
+        assert (Xw[:, :, :col0] == 5.0).all() and (Xw[:, :, col0 + n:] == 5.0).all()
+
+
+@needs_gpu
 def test_input_stage_incoming_row_shard():
     """Incoming mode on a non-square row shard (rows != cols): the transposed planes
     [c][i][k] of this shard's rows k, against the torch stand-in of the same stage."""

@@ -57,7 +57,7 @@ SHARD_BUF_LOCAL, SHARD_BUF_ZSTATS, SHARD_BUF_XBLOCKS, SHARD_BUF_RECV, SHARD_BUF_
 class ShardConfig(ctypes.Structure):
     """Mirror of ftm_shard_config."""
     _fields_ = [("world", _i32), ("rank", _i32), ("scheme", _i32), ("row_chunks", _i32),
-                ("shard", Problem), ("packed", _vp), ("a_local", _vp), ("b_local", _vp),
+                ("shard", Problem), ("packed", _vp), ("a_local", _vp),
                 ("zstats", _vp), ("x_blocks", _vp), ("err_word", _vp),
                 ("recv_a", _vp * MAX_RANKS), ("recv_b", _vp * MAX_RANKS),
                 ("x_plane", _vp * MAX_RANKS), ("flags", _vp * MAX_RANKS)]
@@ -103,7 +103,7 @@ SIGNATURES = {
     "ftm_contraction_general": (ctypes.c_int, [ctypes.POINTER(ContractionLayout), _vp, _vp]),
     "ftm_shard_buffer_bytes": (_sz, [ctypes.POINTER(ShardConfig), ctypes.c_int]),
     "ftm_shard_plan_create": (ctypes.c_int, [ctypes.POINTER(ShardConfig), ctypes.POINTER(_vp)]),
-    "ftm_shard_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "ftm_shard_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _vp]),
     "ftm_shard_plan_destroy": (None, [_vp]),
     "ftm_shard_set_trace": (ctypes.c_int, [_vp, _vp]),
     "ftm_static_scratch_error_word": (_vp, []),

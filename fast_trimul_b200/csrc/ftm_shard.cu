@@ -110,6 +110,7 @@ struct ftm_shard_plan {
   int launches;             // kernels launched by the current forward
   long long* trace;         // optional (time, tag) pairs of the current forward
   int trace_n;
+  ftm_problem out_problem;  // the shard problem with this forward's output dtype
 };
 
 namespace {
@@ -133,7 +134,8 @@ int validate(const ftm_shard_config* c) {
   if (p.rows % c->row_chunks != 0) return FTM_BAD_SHAPE;
   const int rc = p.rows / c->row_chunks;
   if (rc % 128 != 0) return FTM_BAD_SHAPE;   // row / k blocks of the contraction
-  if (kC % c->world != 0 || (kC / c->world) % 8 != 0) return FTM_BAD_SHAPE;
+  // per-destination stores of the input stage: 128 / P channels, a multiple of 16
+  if (kC % c->world != 0 || (kC / c->world) % 16 != 0) return FTM_BAD_SHAPE;
   if (p.mode != FTM_OUTGOING && p.mode != FTM_INCOMING) return FTM_BAD_ARGUMENT;
   return FTM_OK;
 }
@@ -170,6 +172,10 @@ int copy_rows(void* dst, size_t dpitch, const void* src, size_t spitch, size_t w
 
 typedef unsigned short h16;   // fp16 element, for pointer arithmetic
 
+// Owners contracted per launch: with 8 ranks one owner's block is only 128 tiles for
+// 74 CTA pairs, so owners go in pairs there.
+int owners_per_launch(int P) { return P >= 8 ? 2 : 1; }
+
 int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void* out,
                      cudaStream_t cs) {
   const ftm_shard_config& c = pl->cfg;
@@ -177,112 +183,119 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
   const int lq = pl->lq, L = pl->L;
   const bool incoming = c.shard.mode == FTM_INCOMING;
   const size_t unit = pl->unit;                                  // rc * N
-  const size_t blk = size_t(B) * lq * unit;                      // one (src, chunk) block
-  const size_t slot_elems = elems_local(&c);                     // one receive slot
+  const size_t blk = size_t(B) * lq * unit;                      // a (or b) of one (dest, chunk)
+  const size_t slot_elems = 2 * elems_local(&c);                 // a and b of one receive slot
   const int slot = pl->epoch & 1;
   int st;
-  // the previous forward's pushes must be done reading the local planes
+  // Local layout, chunk-major: [chunk r][dest q][a | b][batch][lq][rc][N] (incoming: the
+  // transposed [lq][N][rc] planes), written by the input stage's per-destination stores,
+  // so the a and b pieces rank q needs from chunk r are one contiguous run.
   if ((st = fail(cudaStreamWaitEvent(cs, pl->ev_pushed, 0))) != FTM_OK) return st;
   mark(pl, cs, T_START, 0);
   for (int r = 0; r < RC; ++r) {
     ftm_problem sub = c.shard;
     sub.rows = rc;
-    const size_t chunk = size_t(r) * L * unit;
-    h16* a_r = static_cast<h16*>(c.a_local) + chunk;
-    h16* b_r = static_cast<h16*>(c.b_local) + chunk;
+    h16* chunk = static_cast<h16*>(c.a_local) + size_t(r) * P * 2 * blk;
+    ftm_peer_planes pa{}, pb{};
+    pa.world = pb.world = P;
+    pa.rank = pb.rank = 0;
+    for (int q = 0; q < P; ++q) {
+      pa.base[q] = chunk + size_t(q) * 2 * blk;
+      pb.base[q] = chunk + size_t(q) * 2 * blk + blk;
+    }
     const h16* z_r = static_cast<const h16*>(z) + size_t(r) * rc * N * kC;
     const float* m_r = mask ? mask + size_t(r) * rc * N : nullptr;
-    if ((st = ftm_input_stage(&sub, z_r, m_r, c.packed, a_r, b_r, c.zstats + size_t(r) * rc * N * 2,
-                              c.err_word, cs)) != FTM_OK)
+    if ((st = ftm_input_stage_scatter(&sub, z_r, m_r, c.packed, &pa, &pb,
+                                      c.zstats + size_t(r) * rc * N * 2, c.err_word, cs)) != FTM_OK)
       return st;
     ++pl->launches;
     mark(pl, cs, T_INPUT, r);
     if ((st = fail(cudaEventRecord(pl->ev_in[r], cs))) != FTM_OK) return st;
     if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_in[r], 0))) != FTM_OK) return st;
-    // shifted order: at any moment every rank sends to a different peer
+    // shifted order: at any moment every rank sends to a different peer; own piece last
     for (int sft = 1; sft <= P; ++sft) {
       const int q = (me + sft) % P;
-      const size_t off = size_t(slot) * slot_elems + size_t(me * RC + r) * blk;
-      const size_t src_off = size_t(q) * lq * unit;              // q's channels, batch 0
-      for (int ab = 0; ab < 2; ++ab) {
-        const h16* src = (ab ? b_r : a_r) + src_off;
-        h16* dst = static_cast<h16*>(ab ? c.recv_b[q] : c.recv_a[q]) + off;
-        if ((st = copy_rows(dst, size_t(lq) * unit * 2, src, size_t(kC) * unit * 2,
-                            size_t(lq) * unit * 2, B, pl->copy)) != FTM_OK)
-          return st;
-      }
-      if ((st = signal(pl, q, kFlagAB + me * FTM_SHARD_MAX_ROW_CHUNKS + r)) != FTM_OK) return st;
+      h16* dst = static_cast<h16*>(c.recv_a[q]) + size_t(slot) * slot_elems +
+                 size_t(me * RC + r) * 2 * blk;
+      if ((st = fail(cudaMemcpyAsync(dst, chunk + size_t(q) * 2 * blk, 2 * blk * 2,
+                                     cudaMemcpyDefault, pl->copy))) != FTM_OK)
+        return st;
       mark(pl, pl->copy, T_AB_SENT, q * 16 + r);
     }
+  }
+  // receivers need every chunk before they contract: one flag per peer, raised once
+  for (int sft = 1; sft <= P; ++sft) {
+    const int q = (me + sft) % P;
+    if ((st = signal(pl, q, kFlagAB + me)) != FTM_OK) return st;
   }
   if ((st = fail(cudaEventRecord(pl->ev_pushed, pl->copy))) != FTM_OK) return st;
 
   FlagList fl{};
-  for (int s = 0; s < P; ++s)
-    for (int r = 0; r < RC; ++r) fl.idx[fl.count++] = kFlagAB + s * FTM_SHARD_MAX_ROW_CHUNKS + r;
+  for (int s = 0; s < P; ++s) fl.idx[fl.count++] = kFlagAB + s;
   if ((st = wait_flags(pl, fl, 1, cs)) != FTM_OK) return st;
   mark(pl, cs, T_AB_READY, 0);
   // the previous forward's x pushes must be done reading the x blocks
   if ((st = fail(cudaStreamWaitEvent(cs, pl->ev_x_pushed, 0))) != FTM_OK) return st;
 
-  const h16* Ra = static_cast<const h16*>(c.recv_a[me]) + size_t(slot) * slot_elems;
-  const h16* Rb = static_cast<const h16*>(c.recv_b[me]) + size_t(slot) * slot_elems;
+  // received: [slot][src s][chunk r][a | b][batch][lq][rc][N]
+  const h16* Rs = static_cast<const h16*>(c.recv_a[me]) + size_t(slot) * slot_elems;
   const size_t owner_elems = size_t(B) * lq * R * N;
-  for (int sft = 1; sft <= P; ++sft) {
-    const int o = (me + sft) % P;
+  const int G = owners_per_launch(P), groups = P / G, my_group = me / G;
+  const bool direct_own = (G == 1 && B == 1);
+  for (int gs = 1; gs <= groups; ++gs) {
+    const int g = (my_group + gs) % groups, o0 = g * G;
     ftm_contraction_layout d{};
-    d.L = B * lq; d.m = R; d.n = N; d.k = N;
+    d.L = B * lq; d.m = G * R; d.n = N; d.k = N;
     if (!incoming) {
-      // row blocks (src, chunk) of rc rows; owner o's rows are blocks [o*RC, (o+1)*RC)
+      // row blocks (src, chunk) of rc rows; owners o0.. have blocks [o0*RC, (o0+G)*RC)
       d.k_per_block = N;
-      d.a = Ra + size_t(o) * RC * blk; d.a_rows_per_block = rc;
-      d.a_block_stride = blk; d.a_l_stride = unit; d.a_row_stride = N; d.a_kblock_stride = 0;
-      d.b = Rb; d.b_rows_per_block = rc;
-      d.b_block_stride = blk; d.b_l_stride = unit; d.b_row_stride = N; d.b_kblock_stride = 0;
+      d.a = Rs + size_t(o0) * RC * 2 * blk; d.a_rows_per_block = rc;
+      d.a_block_stride = 2 * blk; d.a_l_stride = unit; d.a_row_stride = N;
+      d.b = Rs + blk; d.b_rows_per_block = rc;
+      d.b_block_stride = 2 * blk; d.b_l_stride = unit; d.b_row_stride = N;
     } else {
-      // k blocks (src, chunk) of rc; planes [l][i][k in block]; owner o's rows i
+      // k blocks (src, chunk) of rc; planes [l][i][k in block]; owners' rows i
       d.k_per_block = rc;
-      d.a = Ra + size_t(o) * R * rc; d.a_rows_per_block = R;
-      d.a_block_stride = 0; d.a_l_stride = unit; d.a_row_stride = rc; d.a_kblock_stride = blk;
-      d.b = Rb; d.b_rows_per_block = N;
-      d.b_block_stride = 0; d.b_l_stride = unit; d.b_row_stride = rc; d.b_kblock_stride = blk;
+      d.a = Rs + size_t(o0) * R * rc; d.a_rows_per_block = G * R;
+      d.a_l_stride = unit; d.a_row_stride = rc; d.a_kblock_stride = 2 * blk;
+      d.b = Rs + blk; d.b_rows_per_block = N;
+      d.b_l_stride = unit; d.b_row_stride = rc; d.b_kblock_stride = 2 * blk;
     }
-    const bool direct = (o == me && B == 1);
+    const bool direct = direct_own && o0 == me;
     d.x = direct ? static_cast<void*>(static_cast<h16*>(c.x_plane[me]) + size_t(me) * lq * R * N)
-                 : static_cast<void*>(static_cast<h16*>(c.x_blocks) + size_t(o) * owner_elems);
-    d.x_rows_per_block = R; d.x_block_stride = 0; d.x_l_stride = size_t(R) * N; d.x_row_stride = N;
+                 : static_cast<void*>(static_cast<h16*>(c.x_blocks) + size_t(o0) * owner_elems);
+    d.x_rows_per_block = R; d.x_block_stride = owner_elems; d.x_l_stride = size_t(R) * N;
+    d.x_row_stride = N;
     if ((st = ftm_contraction_general(&d, c.err_word, cs)) != FTM_OK) return st;
     ++pl->launches;
-    mark(pl, cs, T_CONTRACT, o);
+    mark(pl, cs, T_CONTRACT, g);
     if (direct) continue;
-    if ((st = fail(cudaEventRecord(pl->ev_owner[o], cs))) != FTM_OK) return st;
-    if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_owner[o], 0))) != FTM_OK) return st;
-    h16* dst = static_cast<h16*>(c.x_plane[o]) + size_t(me) * lq * R * N;
-    if ((st = copy_rows(dst, size_t(kC) * R * N * 2, d.x, size_t(lq) * R * N * 2,
-                        size_t(lq) * R * N * 2, B, pl->copy)) != FTM_OK)
-      return st;
+    if ((st = fail(cudaEventRecord(pl->ev_owner[g], cs))) != FTM_OK) return st;
+    if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_owner[g], 0))) != FTM_OK) return st;
+    for (int o = o0; o < o0 + G; ++o) {
+      const h16* src = static_cast<const h16*>(c.x_blocks) + size_t(o) * owner_elems;
+      h16* dst = static_cast<h16*>(c.x_plane[o]) + size_t(me) * lq * R * N;
+      // own block: a local copy on the same stream, ahead of this rank's wait for x
+      if ((st = copy_rows(dst, size_t(kC) * R * N * 2, src, size_t(lq) * R * N * 2,
+                          size_t(lq) * R * N * 2, B, pl->copy)) != FTM_OK)
+        return st;
+      mark(pl, pl->copy, T_X_SENT, o);
+    }
+  }
+  for (int sft = 1; sft <= P; ++sft) {
+    const int o = (me + sft) % P;
+    if (o == me && direct_own) continue;
     if ((st = signal(pl, o, kFlagX + me)) != FTM_OK) return st;
-    mark(pl, pl->copy, T_X_SENT, o);
   }
   if ((st = fail(cudaEventRecord(pl->ev_x_pushed, pl->copy))) != FTM_OK) return st;
   FlagList fx{};
   for (int s = 0; s < P; ++s)
-    if (s != me || B != 1) fx.idx[fx.count++] = kFlagX + s;
-  if (B != 1) {
-    // this rank's own x block still sits in the x blocks: copy it into the plane
-    h16* dst = static_cast<h16*>(c.x_plane[me]) + size_t(me) * lq * R * N;
-    const h16* src = static_cast<const h16*>(c.x_blocks) + size_t(me) * owner_elems;
-    if ((st = copy_rows(dst, size_t(kC) * R * N * 2, src, size_t(lq) * R * N * 2,
-                        size_t(lq) * R * N * 2, B, cs)) != FTM_OK)
-      return st;
-    fx.count = 0;
-    for (int s = 0; s < P; ++s)
-      if (s != me) fx.idx[fx.count++] = kFlagX + s;
-  }
+    if (s != me || !direct_own) fx.idx[fx.count++] = kFlagX + s;
   if (fx.count && (st = wait_flags(pl, fx, 2, cs)) != FTM_OK) return st;
   mark(pl, cs, T_X_READY, 0);
   ++pl->launches;
-  st = ftm_output_stage(&c.shard, z, mask, c.x_plane[me], c.zstats, c.packed, out, c.err_word, cs);
+  st = ftm_output_stage(&pl->out_problem, z, mask, c.x_plane[me], c.zstats, c.packed, out,
+                        c.err_word, cs);
   mark(pl, cs, T_OUTPUT, 0);
   return st;
 }
@@ -351,7 +364,8 @@ int forward_allgather(ftm_shard_plan* pl, const void* z, const float* mask, void
     }
   }
   ++pl->launches;
-  st = ftm_output_stage(&c.shard, z, mask, c.x_blocks, c.zstats, c.packed, out, c.err_word, cs);
+  st = ftm_output_stage(&pl->out_problem, z, mask, c.x_blocks, c.zstats, c.packed, out,
+                        c.err_word, cs);
   mark(pl, cs, T_OUTPUT, 0);
   return st;
 }
@@ -365,11 +379,12 @@ size_t ftm_shard_buffer_bytes(const ftm_shard_config* cfg, int which) {
   const size_t local = elems_local(cfg) * 2;
   const size_t R = size_t(cfg->shard.rows), N = size_t(cfg->shard.cols), B = size_t(cfg->shard.batch);
   switch (which) {
-    case FTM_SHARD_BUF_LOCAL: return local;
+    case FTM_SHARD_BUF_LOCAL:
+      return cfg->scheme == FTM_SHARD_ALLTOALL ? 2 * local : local;
     case FTM_SHARD_BUF_ZSTATS: return B * R * N * 8;
     case FTM_SHARD_BUF_XBLOCKS: return local;
-    case FTM_SHARD_BUF_RECV:
-      return cfg->scheme == FTM_SHARD_ALLGATHER ? 2 * local * size_t(cfg->world) : 2 * local;
+    case FTM_SHARD_BUF_RECV:   // two slots; alltoall: a and b, allgather: b of every rank
+      return cfg->scheme == FTM_SHARD_ALLGATHER ? 2 * local * size_t(cfg->world) : 4 * local;
     case FTM_SHARD_BUF_XPLANE: return local;
     case FTM_SHARD_BUF_FLAGS: return FTM_SHARD_FLAG_WORDS * sizeof(int);
     default: return 0;
@@ -384,10 +399,10 @@ int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
   const bool a2a = cfg->scheme == FTM_SHARD_ALLTOALL;
   if (!cfg->packed || !cfg->a_local || !cfg->zstats || !cfg->x_blocks || !cfg->err_word)
     return FTM_BAD_ARGUMENT;
-  if (a2a && !cfg->b_local) return FTM_BAD_ARGUMENT;
   for (int q = 0; q < cfg->world; ++q) {
-    if (!cfg->recv_b[q] || !cfg->flags[q]) return FTM_BAD_ARGUMENT;
+    if (!cfg->flags[q]) return FTM_BAD_ARGUMENT;
     if (a2a && (!cfg->recv_a[q] || !cfg->x_plane[q])) return FTM_BAD_ARGUMENT;
+    if (!a2a && !cfg->recv_b[q]) return FTM_BAD_ARGUMENT;
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || ftm_device_supported(dev) != 1)
@@ -426,9 +441,12 @@ int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
 }
 
 int ftm_shard_forward(ftm_shard_plan* plan, const void* z, const float* mask, void* out,
-                      ftm_stream_t stream) {
+                      int32_t out_dtype, ftm_stream_t stream) {
   set_last_launch_count(0);
   if (!plan || !z || !out) return FTM_BAD_ARGUMENT;
+  if (out_dtype != FTM_F16 && out_dtype != FTM_BF16 && out_dtype != FTM_F32) return FTM_BAD_DTYPE;
+  plan->out_problem = plan->cfg.shard;
+  plan->out_problem.out_dtype = out_dtype;
   if ((reinterpret_cast<uintptr_t>(z) & 15u) || (reinterpret_cast<uintptr_t>(out) & 15u) ||
       (reinterpret_cast<uintptr_t>(mask) & 15u))
     return FTM_BAD_ALIGN;

@@ -644,7 +644,6 @@ class ShardedTriMul:
         cfg.scheme = _lib.SHARD_ALLTOALL if scheme == "p2p_alltoall" else _lib.SHARD_ALLGATHER
         cfg.row_chunks = self.row_chunks
         cfg.shard = impl.problem(probe, self.out_dtype)
-        self._probs = {self.out_dtype: cfg.shard}
 
         def nbytes(which):
             v = lib.ftm_shard_buffer_bytes(ctypes.byref(cfg), which)
@@ -658,11 +657,10 @@ class ShardedTriMul:
 
         a2a = scheme == "p2p_alltoall"
         self.a_local = buf(_lib.SHARD_BUF_LOCAL)
-        self.b_local = buf(_lib.SHARD_BUF_LOCAL) if a2a else None
         self.zstats = buf(_lib.SHARD_BUF_ZSTATS)
         self.x_blocks = buf(_lib.SHARD_BUF_XBLOCKS)
         self.windows = {}
-        names = ("recv_a", "recv_b", "x_plane", "flags") if a2a else ("recv_b", "flags")
+        names = ("recv_a", "x_plane", "flags") if a2a else ("recv_b", "flags")
         sizes = {"recv_a": _lib.SHARD_BUF_RECV, "recv_b": _lib.SHARD_BUF_RECV,
                  "x_plane": _lib.SHARD_BUF_XPLANE, "flags": _lib.SHARD_BUF_FLAGS}
         for name in names:
@@ -675,7 +673,6 @@ class ShardedTriMul:
         torch.cuda.synchronize(dev)
         cfg.packed = self.packed.data_ptr()
         cfg.a_local = self.a_local.data_ptr()
-        cfg.b_local = self.b_local.data_ptr() if a2a else None
         cfg.zstats = self.zstats.data_ptr()
         cfg.x_blocks = self.x_blocks.data_ptr()
         cfg.err_word = self.errw.ptr
@@ -688,24 +685,8 @@ class ShardedTriMul:
         with torch.cuda.device(dev):
             _lib.check(lib.ftm_shard_plan_create(ctypes.byref(cfg), ctypes.byref(self.plan)),
                        "ftm_shard_plan_create")
-        self._plans = {self.out_dtype: self.plan}
         if self.world > 1:
             dist.barrier(group=group)         # every rank's flags are zero before any push
-
-    def _plan_for(self, out_dtype):
-        """Plans differ only in the output dtype of the problem; one per dtype, sharing
-        every buffer (calls run in stream order, so they never overlap)."""
-        import ctypes
-        if out_dtype not in self._plans:
-            cfg = _lib.ShardConfig.from_buffer_copy(self.cfg)
-            probe = torch.empty(self.batch, self.rows, self.n, C, dtype=self.z_dtype, device="meta")
-            cfg.shard = self.impl.problem(probe, out_dtype)
-            plan = ctypes.c_void_p()
-            with torch.cuda.device(self.device):
-                _lib.check(self.lib.ftm_shard_plan_create(ctypes.byref(cfg), ctypes.byref(plan)),
-                           "ftm_shard_plan_create")
-            self._plans[out_dtype] = plan
-        return self._plans[out_dtype]
 
     def comm_bytes_per_step(self):
         """Bytes this rank sends over NVLink per forward."""
@@ -723,11 +704,13 @@ class ShardedTriMul:
             mask_local = mask_local.to(device=self.device, dtype=torch.float32).expand(shape[:3]).contiguous()
         if out is None:
             out = torch.empty(shape, dtype=self.out_dtype, device=self.device)
+        if out.dtype not in _DTYPES:
+            raise ValueError(f"unsupported output dtype {out.dtype}")
         self.errw.poll()
-        plan = self._plan_for(out.dtype)
-        st = self.lib.ftm_shard_forward(plan, z_local.data_ptr(),
+        st = self.lib.ftm_shard_forward(self.plan, z_local.data_ptr(),
                                         None if mask_local is None else mask_local.data_ptr(),
-                                        out.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+                                        out.data_ptr(), _DTYPES[out.dtype],
+                                        torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(st, "ftm_shard_forward")
         self.last_launches = self.lib.ftm_last_launch_count()
         self.errw.after_launch()
@@ -744,8 +727,10 @@ class ShardedTriMul:
     def enable_trace(self):
         """Record a device-clock timeline of each later forward (ftm_shard_set_trace)."""
         self._trace = torch.zeros(2 * 128, dtype=torch.int64, device=self.device)
-        for plan in self._plans.values():
-            _lib.check(self.lib.ftm_shard_set_trace(plan, self._trace.data_ptr()), "ftm_shard_set_trace")
+        _lib.check(self.lib.ftm_shard_set_trace(self.plan, self._trace.data_ptr()), "ftm_shard_set_trace")
+
+    def disable_trace(self):
+        self.lib.ftm_shard_set_trace(self.plan, None)
 
     def read_trace(self):
         """[(microseconds since the forward's start, event, index)] of the last forward."""
@@ -762,11 +747,14 @@ class ShardedTriMul:
         """Destroy the plans and unmap the peers' windows; call on every rank after the
         last forward, before the process group is destroyed."""
         torch.cuda.synchronize(self.device)
-        for plan in self._plans.values():
-            self.lib.ftm_shard_plan_destroy(plan)
-        self._plans = {}
+        if self.plan:
+            self.lib.ftm_shard_plan_destroy(self.plan)
+            self.plan = None
         for w in self.windows.values():
             w.close()
+
+
+_DTYPES = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 
 
 class _LocalWindow:
@@ -932,8 +920,7 @@ def bench_sharded(args, torch_mod):
         allt = [None] * world
         dist.all_gather_object(allt, mine)
         trace = allt
-        for plan in sh._plans.values():
-            sh.lib.ftm_shard_set_trace(plan, None)
+        sh.disable_trace()
     ms = torch.tensor([t0.elapsed_time(t1) / K], device=dev)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     clocks = clk.summary()

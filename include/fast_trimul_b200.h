@@ -224,16 +224,16 @@ int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes*
  * as mapped in this process (this rank's own entry is its local buffer); flags must be
  * zeroed before the first forward. The plan owns one copy stream and a few events (no
  * device memory). Requirements: rows % row_chunks == 0, rows / row_chunks % 128 == 0,
- * (128 / P) % 8 == 0, row_chunks == 1 when batch > 1. */
+ * (128 / P) % 16 == 0 (P <= 8), row_chunks == 1 when batch > 1. */
 #define FTM_SHARD_ALLTOALL 0
 #define FTM_SHARD_ALLGATHER 1
 #define FTM_SHARD_MAX_ROW_CHUNKS 8
 #define FTM_SHARD_FLAG_WORDS 256
 enum {
-  FTM_SHARD_BUF_LOCAL = 0,   /* a_local, b_local: this rank's projections, chunk-major */
+  FTM_SHARD_BUF_LOCAL = 0,   /* a_local: this rank's projections (alltoall: a and b), chunk-major */
   FTM_SHARD_BUF_ZSTATS = 1,  /* zstats */
   FTM_SHARD_BUF_XBLOCKS = 2, /* x_blocks: alltoall -- x per row owner; allgather -- x plane */
-  FTM_SHARD_BUF_RECV = 3,    /* each receive window (two slots) */
+  FTM_SHARD_BUF_RECV = 3,    /* each receive window (two slots; alltoall: a and b in recv_a) */
   FTM_SHARD_BUF_XPLANE = 4,  /* each x plane (alltoall) */
   FTM_SHARD_BUF_FLAGS = 5    /* each flag buffer */
 };
@@ -244,20 +244,21 @@ typedef struct {
   ftm_problem shard;    /* this rank's rows: rows = N / world, cols = N */
   const void* packed;
   void* a_local;
-  void* b_local;        /* alltoall only */
   float* zstats;
   void* x_blocks;
   int* err_word;
-  void* recv_a[FTM_MAX_RANKS];   /* alltoall only */
-  void* recv_b[FTM_MAX_RANKS];
+  void* recv_a[FTM_MAX_RANKS];   /* alltoall: a and b arrive here */
+  void* recv_b[FTM_MAX_RANKS];   /* allgather: b of every rank arrives here */
   void* x_plane[FTM_MAX_RANKS];  /* alltoall only */
   int* flags[FTM_MAX_RANKS];
 } ftm_shard_config;
 typedef struct ftm_shard_plan ftm_shard_plan;
 size_t ftm_shard_buffer_bytes(const ftm_shard_config* cfg, int which);
 int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan);
+/* out_dtype: FTM_F16, FTM_BF16 or FTM_F32 (shard.out_dtype is the default a caller
+ * normally passes). */
 int ftm_shard_forward(ftm_shard_plan* plan, const void* z, const float* mask, void* out,
-                      ftm_stream_t stream);
+                      int32_t out_dtype, ftm_stream_t stream);
 void ftm_shard_plan_destroy(ftm_shard_plan* plan);
 /* Optional timeline of the following forwards (for profiling): `trace` is a device buffer
  * of 2 * FTM_SHARD_TRACE_POINTS int64; each forward overwrites it with (device clock ns,

@@ -837,6 +837,9 @@ def main():
                     help="skip timing the reference's own GPU kernels (reference_gpu key)")
     ap.add_argument("--trace", action="store_true",
                     help="N>1: add the device-clock timeline of one forward per rank (trace key)")
+    ap.add_argument("--push", default=None, choices=["ce", "sm"],
+                    help="N>1: pushes of the native pipeline by copy engines (ce) or by a kernel "
+                         "of vector stores (sm)")
     ap.add_argument("--row-chunks", type=int, default=None,
                     help="input-stage row chunks of the native sharded pipeline (N>1)")
     ap.add_argument("--chunks", type=int, default=None,
@@ -875,6 +878,8 @@ def main():
         return
 
     import torch
+    if args.push:
+        os.environ["FTM_SHARD_PUSH"] = args.push
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1 or args.gpus > 1:
         from fast_trimul_b200.distributed import bench_sharded

@@ -85,6 +85,50 @@ __global__ void signal_kernel(int* flag, int epoch) {
   st_release_sys(flag, epoch);
 }
 
+// SM-driven push: copies up to kMaxSegs (src, dst) runs of 16-byte words -- dst usually
+// in a peer's memory -- with every CTA taking a strided share of each run, four words in
+// flight per thread. With `nflags` > 0 the last CTA to finish raises each flag to
+// `epoch` after all CTAs' stores are fenced at system scope.
+constexpr int kMaxSegs = 64;
+struct PushList {
+  const uint4* src[kMaxSegs];
+  uint4* dst[kMaxSegs];
+  unsigned long long n16[kMaxSegs];
+  int* flag[FTM_MAX_RANKS];
+  int count, nflags, epoch;
+  unsigned int* done;   // CTA counter (zero between launches)
+};
+
+__global__ void __launch_bounds__(256) push_kernel(const __grid_constant__ PushList pl) {
+  const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+  const unsigned long long t0 = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int s = 0; s < pl.count; ++s) {
+    const uint4* __restrict__ src = pl.src[s];
+    uint4* dst = pl.dst[s];
+    const unsigned long long n = pl.n16[s];
+    unsigned long long i = t0;
+    for (; i + 3 * stride < n; i += 4 * stride) {
+      const uint4 v0 = __ldg(src + i), v1 = __ldg(src + i + stride);
+      const uint4 v2 = __ldg(src + i + 2 * stride), v3 = __ldg(src + i + 3 * stride);
+      dst[i] = v0;
+      dst[i + stride] = v1;
+      dst[i + 2 * stride] = v2;
+      dst[i + 3 * stride] = v3;
+    }
+    for (; i < n; i += stride) dst[i] = __ldg(src + i);
+  }
+  if (pl.nflags == 0) return;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(pl.done, 1u) == gridDim.x - 1) {
+      __threadfence_system();
+      for (int f = 0; f < pl.nflags; ++f) st_release_sys(pl.flag[f], pl.epoch);
+      *pl.done = 0;
+    }
+  }
+}
+
 // Trace point (only when a trace buffer is configured): records the device clock when
 // everything queued before it on its stream has finished.
 __global__ void mark_kernel(long long* trace, int slot, int tag) {
@@ -111,6 +155,10 @@ struct ftm_shard_plan {
   long long* trace;         // optional (time, tag) pairs of the current forward
   int trace_n;
   ftm_problem out_problem;  // the shard problem with this forward's output dtype
+  int sm_push;              // pushes by push_kernel (FTM_SHARD_PUSH=sm) instead of copy engines
+  int push_ctas;
+  unsigned int* push_done;  // counter for push_kernel (the plan's config scratch)
+  PushList pending;         // runs queued for the next push
 };
 
 namespace {
@@ -163,14 +211,48 @@ int signal(ftm_shard_plan* pl, int q, int word) {
   return fail(cudaGetLastError());
 }
 
-// B rows of `width` bytes (1 row when B == 1): a plain peer copy or a 2-D one
-int copy_rows(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, int rows,
-              cudaStream_t s) {
-  if (rows == 1) return fail(cudaMemcpyAsync(dst, src, width, cudaMemcpyDefault, s));
-  return fail(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, cudaMemcpyDefault, s));
+typedef unsigned short h16;   // fp16 element, for pointer arithmetic
+
+// Queue one run (bytes a multiple of 16) for the plan's push path: a copy-engine copy
+// right away, or a run of the next push_kernel launch.
+int push_run(ftm_shard_plan* pl, void* dst, const void* src, size_t bytes) {
+  if (!pl->sm_push) return fail(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, pl->copy));
+  PushList& p = pl->pending;
+  if (p.count == kMaxSegs) return FTM_BAD_ARGUMENT;
+  p.src[p.count] = static_cast<const uint4*>(src);
+  p.dst[p.count] = static_cast<uint4*>(dst);
+  p.n16[p.count] = bytes / 16;
+  ++p.count;
+  return FTM_OK;
 }
 
-typedef unsigned short h16;   // fp16 element, for pointer arithmetic
+// Launch the queued runs (SM path) and raise `flags` of the peers in `who` (bit q) to
+// the forward's epoch once they have landed; on the copy-engine path the runs are
+// already queued and the flags are raised by signal kernels.
+int push_flush(ftm_shard_plan* pl, unsigned who, int word) {
+  int st;
+  if (!pl->sm_push) {
+    for (int sft = 1; sft <= pl->P; ++sft) {
+      const int q = (pl->me + sft) % pl->P;
+      if (who & (1u << q))
+        if ((st = signal(pl, q, word)) != FTM_OK) return st;
+    }
+    return FTM_OK;
+  }
+  PushList& p = pl->pending;
+  p.nflags = 0;
+  for (int q = 0; q < pl->P; ++q)
+    if (who & (1u << q)) p.flag[p.nflags++] = pl->cfg.flags[q] + word;
+  p.epoch = pl->epoch;
+  p.done = pl->push_done;
+  if (p.count || p.nflags) {
+    push_kernel<<<pl->push_ctas, 256, 0, pl->copy>>>(p);
+    ++pl->launches;
+    if ((st = fail(cudaGetLastError())) != FTM_OK) return st;
+  }
+  p.count = 0;
+  return FTM_OK;
+}
 
 // Owners contracted per launch: with 8 ranks one owner's block is only 128 tiles for
 // 74 CTA pairs, so owners go in pairs there.
@@ -180,7 +262,7 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
                      cudaStream_t cs) {
   const ftm_shard_config& c = pl->cfg;
   const int P = pl->P, me = pl->me, RC = pl->RC, rc = pl->rc, R = pl->R, N = pl->N, B = pl->B;
-  const int lq = pl->lq, L = pl->L;
+  const int lq = pl->lq;
   const bool incoming = c.shard.mode == FTM_INCOMING;
   const size_t unit = pl->unit;                                  // rc * N
   const size_t blk = size_t(B) * lq * unit;                      // a (or b) of one (dest, chunk)
@@ -217,16 +299,13 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
       const int q = (me + sft) % P;
       h16* dst = static_cast<h16*>(c.recv_a[q]) + size_t(slot) * slot_elems +
                  size_t(me * RC + r) * 2 * blk;
-      if ((st = fail(cudaMemcpyAsync(dst, chunk + size_t(q) * 2 * blk, 2 * blk * 2,
-                                     cudaMemcpyDefault, pl->copy))) != FTM_OK)
-        return st;
-      mark(pl, pl->copy, T_AB_SENT, q * 16 + r);
+      if ((st = push_run(pl, dst, chunk + size_t(q) * 2 * blk, 2 * blk * 2)) != FTM_OK) return st;
+      if (!pl->sm_push) mark(pl, pl->copy, T_AB_SENT, q * 16 + r);
     }
-  }
-  // receivers need every chunk before they contract: one flag per peer, raised once
-  for (int sft = 1; sft <= P; ++sft) {
-    const int q = (me + sft) % P;
-    if ((st = signal(pl, q, kFlagAB + me)) != FTM_OK) return st;
+    // receivers need every chunk before they contract: one flag per peer, raised after
+    // the last chunk
+    if ((st = push_flush(pl, r == RC - 1 ? (1u << P) - 1 : 0u, kFlagAB + me)) != FTM_OK) return st;
+    if (pl->sm_push) mark(pl, pl->copy, T_AB_SENT, r);
   }
   if ((st = fail(cudaEventRecord(pl->ev_pushed, pl->copy))) != FTM_OK) return st;
 
@@ -276,17 +355,22 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
       const h16* src = static_cast<const h16*>(c.x_blocks) + size_t(o) * owner_elems;
       h16* dst = static_cast<h16*>(c.x_plane[o]) + size_t(me) * lq * R * N;
       // own block: a local copy on the same stream, ahead of this rank's wait for x
-      if ((st = copy_rows(dst, size_t(kC) * R * N * 2, src, size_t(lq) * R * N * 2,
-                          size_t(lq) * R * N * 2, B, pl->copy)) != FTM_OK)
-        return st;
-      mark(pl, pl->copy, T_X_SENT, o);
+      for (int b = 0; b < B; ++b)
+        if ((st = push_run(pl, dst + size_t(b) * kC * R * N, src + size_t(b) * lq * R * N,
+                           size_t(lq) * R * N * 2)) != FTM_OK)
+          return st;
+      if (!pl->sm_push) mark(pl, pl->copy, T_X_SENT, o);
+    }
+    if (pl->sm_push) {
+      if ((st = push_flush(pl, 0u, 0)) != FTM_OK) return st;
+      mark(pl, pl->copy, T_X_SENT, g);
     }
   }
-  for (int sft = 1; sft <= P; ++sft) {
-    const int o = (me + sft) % P;
-    if (o == me && direct_own) continue;
-    if ((st = signal(pl, o, kFlagX + me)) != FTM_OK) return st;
-  }
+  // owners wait for every source's x: one flag per owner, after the last push
+  unsigned who = 0;
+  for (int o = 0; o < P; ++o)
+    if (!(o == me && direct_own)) who |= 1u << o;
+  if ((st = push_flush(pl, who, kFlagX + me)) != FTM_OK) return st;
   if ((st = fail(cudaEventRecord(pl->ev_x_pushed, pl->copy))) != FTM_OK) return st;
   FlagList fx{};
   for (int s = 0; s < P; ++s)
@@ -330,9 +414,9 @@ int forward_allgather(ftm_shard_plan* pl, const void* z, const float* mask, void
     for (int sft = 1; sft < P; ++sft) {
       const int q = (me + sft) % P;
       h16* dst = static_cast<h16*>(c.recv_b[q]) + size_t(slot) * slot_elems + size_t(me * RC + r) * blk;
-      if ((st = fail(cudaMemcpyAsync(dst, b_r, blk * 2, cudaMemcpyDefault, pl->copy))) != FTM_OK)
+      if ((st = push_run(pl, dst, b_r, blk * 2)) != FTM_OK) return st;
+      if ((st = push_flush(pl, 1u << q, kFlagAB + me * FTM_SHARD_MAX_ROW_CHUNKS + r)) != FTM_OK)
         return st;
-      if ((st = signal(pl, q, kFlagAB + me * FTM_SHARD_MAX_ROW_CHUNKS + r)) != FTM_OK) return st;
       mark(pl, pl->copy, T_AB_SENT, q * 16 + r);
     }
   }
@@ -422,6 +506,19 @@ int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
   pl->unit = size_t(pl->rc) * pl->N;
   pl->dev = dev;
   pl->epoch = 0;
+  // FTM_SHARD_PUSH=sm: pushes by a kernel of FTM_SHARD_PUSH_CTAS CTAs (default 32) doing
+  // vector stores into the peers' windows, instead of copy-engine copies
+  {
+    const char* v = getenv("FTM_SHARD_PUSH");
+    pl->sm_push = (v && strcmp(v, "sm") == 0) ? 1 : 0;
+    const char* n = getenv("FTM_SHARD_PUSH_CTAS");
+    pl->push_ctas = n ? atoi(n) : 32;
+    if (pl->push_ctas < 1) pl->push_ctas = 1;
+    if (pl->push_ctas > 1024) pl->push_ctas = 1024;
+    // the counter lives in the last word of this rank's flag buffer (zeroed by the caller,
+    // never written by peers)
+    pl->push_done = reinterpret_cast<unsigned int*>(cfg->flags[cfg->rank] + FTM_SHARD_FLAG_WORDS - 1);
+  }
   bool ok = cudaStreamCreateWithFlags(&pl->copy, cudaStreamNonBlocking) == cudaSuccess;
   for (int i = 0; ok && i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
     ok = cudaEventCreateWithFlags(&pl->ev_in[i], cudaEventDisableTiming) == cudaSuccess;

@@ -885,7 +885,8 @@ def bench_sharded(args, torch_mod):
                            row_chunks=getattr(args, "row_chunks", None))
         run = sh
         check = sh.check
-        detail = {"scheme": scheme, "row_chunks": sh.row_chunks}
+        detail = {"scheme": scheme, "row_chunks": sh.row_chunks,
+                  "push": os.environ.get("FTM_SHARD_PUSH", "ce")}
     else:
         chunks = getattr(args, "chunks", None) or (4 if scheme.startswith("allgather") else 2)
         sh = RowShardedTriMul(layer._impl, 1, n, chunks=chunks, device=dev, scheme=scheme)

@@ -24,8 +24,9 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, path, scheme, mode="outgoing", row_chunks=None):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+def _worker(rank, world, port, path, scheme, mode="outgoing", row_chunks=None, push="ce"):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      FTM_SHARD_PUSH=push)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
@@ -64,7 +65,7 @@ def _worker(rank, world, port, path, scheme, mode="outgoing", row_chunks=None):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("scheme,mode", [("p2p_allgather", "outgoing"), ("p2p_alltoall", "outgoing"),
-                                         ("p2p_alltoall", "incoming"),
+                                         ("p2p_alltoall", "incoming"), ("p2p_alltoall_sm", "outgoing"),
                                          ("allgather", "outgoing"), ("alltoall", "outgoing"),
                                          ("allgather_ce", "outgoing"), ("alltoall_ce", "outgoing"),
                                          ("fused", "outgoing"), ("alltoall_ce", "incoming"),
@@ -72,8 +73,10 @@ def _worker(rank, world, port, path, scheme, mode="outgoing", row_chunks=None):
 def test_two_gpu_row_sharding(tmp_path, scheme, mode):
     from tests.helpers import MAX_ABS, MEAN_REL, compare, make_layer, oracle_out
     path = str(tmp_path / "o.npy")
-    mp.start_processes(_worker, args=(2, _free_port(), path, scheme, mode), nprocs=2, join=True,
-                       start_method="spawn")
+    push = "sm" if scheme.endswith("_sm") else "ce"
+    scheme = scheme[:-3] if scheme.endswith("_sm") else scheme
+    mp.start_processes(_worker, args=(2, _free_port(), path, scheme, mode, None, push), nprocs=2,
+                       join=True, start_method="spawn")
     got = torch.from_numpy(np.load(path))
     m = make_layer(mode, True)
     gen = torch.Generator().manual_seed(21)
@@ -99,16 +102,19 @@ def test_single_rank_sharded_object_matches_plain_forward():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
-@pytest.mark.parametrize("scheme,mode,row_chunks", [("p2p_alltoall", "outgoing", 2),
-                                                    ("p2p_alltoall", "incoming", 2),
-                                                    ("p2p_allgather", "outgoing", 2),
-                                                    ("p2p_alltoall", "outgoing", 1)])
-def test_single_rank_native_pipeline(scheme, mode, row_chunks):
+@pytest.mark.parametrize("scheme,mode,row_chunks,push", [("p2p_alltoall", "outgoing", 2, "ce"),
+                                                         ("p2p_alltoall", "incoming", 2, "ce"),
+                                                         ("p2p_allgather", "outgoing", 2, "ce"),
+                                                         ("p2p_alltoall", "outgoing", 1, "ce"),
+                                                         ("p2p_alltoall", "outgoing", 2, "sm"),
+                                                         ("p2p_allgather", "outgoing", 2, "sm")])
+def test_single_rank_native_pipeline(scheme, mode, row_chunks, push, monkeypatch):
     """world = 1: the native pipeline (row-chunked input stage, copies into its own
     receive window, flag waits, strided contractions) equals the plain forward, over
     several forwards (alternating receive slots, increasing flag epochs)."""
     from fast_trimul_b200.distributed import ShardedTriMul
     from tests.helpers import make_layer
+    monkeypatch.setenv("FTM_SHARD_PUSH", push)
     m = make_layer(mode, True).cuda()
     g = torch.Generator(device="cuda").manual_seed(22)
     sh = ShardedTriMul(m._impl, 1, 256, device="cuda", out_dtype=torch.float32, scheme=scheme,

@@ -498,12 +498,35 @@ def bench_trunk(args, torch, dev, n=384, blocks=8):
                 ts.append(a.elapsed_time(b))
         return statistics.median(ts), out
 
+    def trimul_layers_ms(model):
+        """The trunk's 16 TriMul layers alone, each on the trunk's input z and mask."""
+        layers = [m for blk in model.blocks for m in (blk.tri_out, blk.tri_in)]
+        with torch.no_grad():
+            for lay in layers:
+                lay(z, mask=mask)
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(5):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for lay in layers:
+                    lay(z, mask=mask)
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
     ms_ref, (s_ref, z_ref) = timed(ref)
     ms_fast, (s_fast, z_fast) = timed(fast)
+    tri_ref, tri_fast = trimul_layers_ms(ref), trimul_layers_ms(fast)
     dz = ((z_fast.float() - z_ref.float()).abs().mean() / z_ref.float().abs().mean()).item()
     return {"config": "C4 PairFormer-style trunk, 8 blocks, N=384, c_s=384, c_z=128, bf16",
             "ms_per_fwd_torch_trimul": round(ms_ref, 3), "ms_per_fwd_fast_trimul": round(ms_fast, 3),
             "speedup": round(ms_ref / ms_fast, 3),
+            "trimul_layers_ms": {"torch": round(tri_ref, 3), "fast": round(tri_fast, 3)},
+            "trimul_share_of_trunk": {"torch": round(tri_ref / ms_ref, 3),
+                                      "fast": round(tri_fast / ms_fast, 3)},
+            "mask_semantics": "both trunks: z * mask before the input LayerNorm, output * mask",
             "trimul_tflop_per_fwd": round(trunk_flops_trimul(n, C, blocks) / 1e12, 4),
             "z_out_mean_rel_diff": round(dz, 5)}
 

@@ -22,7 +22,10 @@ import torch.nn.functional as F
 
 class TriMulTorch(nn.Module):
     """Plain PyTorch triangle multiplicative update (delta only): the unaccelerated
-    layer the trunk is compared against. Mask on a/b as the model libraries apply it."""
+    layer the trunk is compared against. The pair mask is applied with the same rules as
+    the accelerated layer (the reference's functional entry, functional.py:19-26): z is
+    multiplied by the mask before the input LayerNorm and the result by the mask again,
+    so the two trunks compute the same function with or without a mask."""
 
     def __init__(self, c_z, c_h=None, mode="outgoing"):
         super().__init__()
@@ -36,16 +39,18 @@ class TriMulTorch(nn.Module):
         self.gate_out = nn.Linear(c_z, c_z)
 
     def forward(self, z, mask=None):
+        m = None if mask is None else mask.unsqueeze(-1).to(z.dtype)
+        if m is not None:
+            z = z * m
         zn = self.norm_in(z)
         ab = self.proj_ab(zn) * torch.sigmoid(self.gate_ab(zn))
-        if mask is not None:
-            ab = ab * mask.unsqueeze(-1)
         a, b = ab.chunk(2, dim=-1)
         if self.mode == "outgoing":
             x = torch.einsum("bikc,bjkc->bijc", a, b)
         else:
             x = torch.einsum("bkic,bkjc->bijc", a, b)
-        return torch.sigmoid(self.gate_out(zn)) * self.proj_out(self.norm_out(x))
+        out = torch.sigmoid(self.gate_out(zn)) * self.proj_out(self.norm_out(x))
+        return out if m is None else out * m
 
 
 class TriangleAttention(nn.Module):

@@ -16,10 +16,14 @@ def test_trimul_torch_matches_fast_layer():
     src.blocks[0].tri_in = ref
     copy_trimul_weights(src, dst)
     z = torch.randn(1, 12, 12, 32)
+    mask = torch.ones(1, 12, 12)
+    mask[:, 10:] = 0
+    mask[:, :, 10:] = 0
     with torch.no_grad():
-        want = ref(z)
-        got = dst.blocks[0].tri_in(z)
-    assert (got.float() - want).abs().max() < 2e-2
+        for mk in (None, mask):
+            want = ref(z, mask=mk)
+            got = dst.blocks[0].tri_in(z, mask=mk)
+            assert (got.float() - want).abs().max() < 2e-2
 
 
 def test_trunk_swap_preserves_output():

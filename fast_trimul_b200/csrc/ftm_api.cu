@@ -404,6 +404,11 @@ WsLayout ws_layout(const ftm_problem* p) {
 
 namespace ftm {
 
+bool pdl_enabled() {
+  const char* v = getenv("FTM_PDL");
+  return !(v && strcmp(v, "0") == 0);
+}
+
 int check_forward_args(const ftm_problem* p, const void* z, const float* mask, const void* packed,
                        const void* out) {
   const int st = check_problem(p);

@@ -118,6 +118,17 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
   return __all_sync(0xffffffffu, ok);
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while its predecessor on the stream is still finishing; it
+// must not touch global memory (other than prefetching tensor-map descriptors) before
+// grid_dep_wait(), which returns once the predecessor grid has completed and its writes
+// are visible. Each kernel releases its own dependents only after that wait, so a
+// kernel can never overlap anything but the tail of its immediate predecessor.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ bool grid_failed(const int* err) {
   return *reinterpret_cast<const volatile int*>(err) != 0;
 }

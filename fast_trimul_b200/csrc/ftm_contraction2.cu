@@ -145,6 +145,8 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dep_wait();     // operands written, X free
+  grid_dep_release();
 
   const int tiles_m = (M + 2 * kBM - 1) / (2 * kBM);
   const int tiles_n = (N + 2 * kBN * NH - 1) / (2 * kBN * NH);
@@ -344,21 +346,13 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
     if (e != cudaSuccess) return e;
     const long tiles = long(L) * ((M + 255) / 256) * ((N + tile_n - 1) / tile_n);
     const int clusters = static_cast<int>(tiles < num_sms / 2 ? tiles : num_sms / 2);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes;
-    cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, amap, bmap, X, L, M, N, K, lay, err, xd);
-    if (e != cudaSuccess) return e;
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(2 * clusters), dim3(kThreads), smem_bytes, stream, attr, 1, amap,
+                      bmap, X, L, M, N, K, lay, err, xd);
   };
   if (nh == 2) return go(contraction_pair_kernel<2>, PairCfg<2>::kSmemBytes, 512);
   return go(contraction_pair_kernel<1>, PairCfg<1>::kSmemBytes, 256);

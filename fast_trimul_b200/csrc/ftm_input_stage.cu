@@ -87,6 +87,8 @@ input_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dep_wait();      // z, mask, weights and the buffers this stage writes are free now
+  grid_dep_release();
 
   const int ntiles = tl.tiles;
 
@@ -345,10 +347,9 @@ cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
   cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  input_stage_kernel<<<grid, kInThreads, kSmemBytes, stream>>>(zmap, wmap, smaps, mask, u_in,
-                                                               v_in, zstats, tl, incoming, z_bf16,
-                                                               eps, err, test_stall);
-  return cudaGetLastError();
+  return launch_pdl(input_stage_kernel, dim3(grid), dim3(kInThreads), kSmemBytes, stream, nullptr, 0,
+                    zmap, wmap, smaps, mask, u_in, v_in, zstats, tl, incoming, z_bf16, eps, err,
+                    test_stall);
 }
 
 }  // namespace ftm

@@ -10,6 +10,32 @@
 
 namespace ftm {
 
+// Launch with programmatic stream serialisation (FTM_PDL=0 turns it off): the kernel's
+// set-up overlaps the tail of the previous kernel on the stream; the kernels call
+// grid_dep_wait() before their first global access.
+bool pdl_enabled();
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       const cudaLaunchAttribute* extra, int n_extra, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[4];
+  int n = 0;
+  for (int i = 0; i < n_extra && n < 3; ++i) attr[n++] = extra[i];
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 // Packed parameter buffer (built by ftm_pack_params), byte offsets for C = c_z = c_h.
 struct PackedLayout {
   size_t w_in, w_out, u_in, v_in, u_g, v_g, u_o, v_o, total;

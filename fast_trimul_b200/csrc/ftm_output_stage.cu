@@ -120,6 +120,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
     mbar_init(mma_drain, 1);
     fence_mbar_init();
   }
+  grid_dep_wait();      // x, z statistics, weights and the output buffer are ready / free
   for (int k = threadIdx.x; k < kC / 2; k += blockDim.x) {
     sUV[2 * k] = make_float4(0.5f * u_g[2 * k], 0.5f * u_g[2 * k + 1], 0.5f * v_g[2 * k], 0.5f * v_g[2 * k + 1]);
     sUV[2 * k + 1] = make_float4(u_o[2 * k], u_o[2 * k + 1], v_o[2 * k], v_o[2 * k + 1]);
@@ -130,6 +131,7 @@ output_stage_kernel(const __grid_constant__ CUtensorMap zmap,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int ntiles = tl.tiles;
+  grid_dep_release();
 
   if (warp == 0) {
     // two producer lanes: lane 0 refills x halves as soon as the MMA has read them,
@@ -443,9 +445,9 @@ cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kOutThreads, kSmemBytes, stream>>>(zmap, xmap, wmap, omap, mask, zstats, u_g, v_g, u_o, v_o, out,
-                                                    tl, residual, z_bf16, eps_in, eps_out, err);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(grid), dim3(kOutThreads), kSmemBytes, stream, nullptr, 0, zmap, xmap,
+                      wmap, omap, mask, zstats, u_g, v_g, u_o, v_o, out, tl, residual, z_bf16,
+                      eps_in, eps_out, err);
   };
   switch (out_dtype) {
     case 0: return go(output_stage_kernel<0>);

@@ -93,3 +93,39 @@ def test_gradients_are_finite():
     assert z.grad is not None and torch.isfinite(z.grad).all()
     grads = [p.grad for p in m._impl.parameters()]
     assert all(g is not None and torch.isfinite(g).all() for g in grads)
+
+
+@needs_gpu
+@pytest.mark.parametrize("mode", ["outgoing", "incoming"])
+def test_gradients_match_fp32_autograd(mode):
+    """Gradients of z and of all 16 parameters through the layer's training path match
+    torch autograd of the fp32 module (the reference formula, _kernels.py:532-547, on
+    fp32 copies of the same fp16 weights) with the same mask rules. Tolerance: the
+    gradient's max-abs error relative to its largest entry, at fp16-storage level."""
+    import torch.nn.functional as F  # noqa: F401
+    m = make_layer(mode, True).cuda()
+    z, mask = _inputs(48, 37, dtype=torch.float32)
+    z, mask = z.cuda(), mask.cuda()
+    g = torch.Generator(device="cuda").manual_seed(38)
+    gout = torch.randn(z.shape, device="cuda", generator=g)
+    zq = z.clone().requires_grad_(True)
+    out = m(zq, mask=mask)
+    out.float().backward(gout)
+    got = [zq.grad] + [p.grad for p in m._impl._params()]
+
+    ref = make_layer(mode, True).cuda()
+    ref._impl.load_state_dict({k: v.float() for k, v in m._impl.state_dict().items()})
+    ref._impl.float()
+    params = [p.detach().clone().requires_grad_(True) for p in ref._impl._params()]
+    zr = z.clone().requires_grad_(True)
+    mm = mask.unsqueeze(-1)
+    o = ref._impl._torch_forward(zr * mm, params) * mm
+    o.backward(gout)
+    want = [zr.grad] + [p.grad for p in params]
+    from oracle.trimul_oracle import PARAM_NAMES       # the _params() order
+    names = ["z"] + list(PARAM_NAMES)
+    for name, a, b in zip(names, got, want):
+        assert a is not None and torch.isfinite(a).all(), name
+        scale = b.abs().max().item()
+        err = (a.float() - b).abs().max().item()
+        assert err <= 2e-2 * scale + 1e-6, (name, err, scale)

@@ -72,7 +72,8 @@ class ContractionLayout(ctypes.Structure):
                 ("b", _vp), ("b_rows_per_block", _i32), ("b_block_stride", _i64),
                 ("b_l_stride", _i64), ("b_row_stride", _i64), ("b_kblock_stride", _i64),
                 ("x", _vp), ("x_rows_per_block", _i32), ("x_block_stride", _i64),
-                ("x_l_stride", _i64), ("x_row_stride", _i64)]
+                ("x_l_stride", _i64), ("x_row_stride", _i64),
+                ("a_mn_major", _i32), ("b_mn_major", _i32)]
 
 
 _PP = ctypes.POINTER(Problem)

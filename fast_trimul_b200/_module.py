@@ -182,7 +182,7 @@ class TriangleMultiplicativeUpdateKernelFused(nn.Module):
                             1 if self.residual else 0, _DT[z.dtype], _DT[out_dtype],
                             float(self.norm_in.eps), float(self.norm_out.eps))
 
-    def _forward_native(self, z, mask=None, out_dtype=None):
+    def _forward_native(self, z, mask=None, out_dtype=None, keep_planes=False):
         """z: (B, N, N, d_z) CUDA tensor (fp16/bf16; fp32 is converted to fp16 like
         functional.py:23); mask: (B, N, N) or None. Returns z's dtype unless
         `out_dtype` says otherwise. Mask semantics are applied inside the kernels.
@@ -225,6 +225,12 @@ class TriangleMultiplicativeUpdateKernelFused(nn.Module):
         errw.after_launch()
         _lib.stats["calls"] += 1
         _lib.stats["kernel_launches"] += 3
+        if keep_planes:
+            # fp16 channel-major a, b, x (B, C, N, N) for the backward (views of ws)
+            n_el = B * self.d_c * N * N
+            views = tuple(ws[off:off + 2 * n_el].view(torch.float16).view(B, self.d_c, N, N)
+                          for off in (0, plane, 2 * plane))
+            return out, views
         return out
 
     def check(self, device=None):
@@ -243,30 +249,28 @@ class TriangleMultiplicativeUpdateKernelFused(nn.Module):
 
 
 class _TrainableTriMul(torch.autograd.Function):
-    """Native forward, torch-recompute backward (the reference's _kernels.py:468-488)."""
+    """Native forward that keeps the planes a, b, x; backward with the contraction's
+    gradients on the native kernel and the per-position parts recomputed in fp32
+    (fast_trimul_b200.backward). Replaces the reference's recompute-everything
+    backward (_kernels.py:468-488)."""
 
     @staticmethod
     def forward(ctx, mod, z, mask, *params):
         ctx.mod = mod
         ctx.has_mask = mask is not None
-        ctx.save_for_backward(z, *([mask] if mask is not None else []), *params)
         with torch.no_grad():
-            return mod._forward_native(z, mask)
+            out, planes = mod._forward_native(z, mask, keep_planes=True)
+        ctx.save_for_backward(z, *([mask] if mask is not None else []), *params, *planes)
+        return out
 
     @staticmethod
     def backward(ctx, grad_out):
+        from .backward import backward as native_backward
         saved = ctx.saved_tensors
-        z = saved[0].detach().requires_grad_(True)
+        z = saved[0]
         mask = saved[1] if ctx.has_mask else None
-        params = [t.detach().requires_grad_(True) for t in saved[(2 if ctx.has_mask else 1):]]
-        with torch.enable_grad():
-            zz = z.to(params[0].dtype)
-            if mask is not None:
-                m = mask.unsqueeze(-1).to(zz.dtype)
-                zz = zz * m
-            out = ctx.mod._torch_forward(zz, params)
-            if mask is not None:
-                out = out * m
-        grads = torch.autograd.grad(out, [z] + params, grad_out.to(out.dtype), allow_unused=True)
-        return (None, grads[0], None, *grads[1:])
-
+        first = 2 if ctx.has_mask else 1
+        params = list(saved[first:first + 16])
+        planes = saved[first + 16:first + 19]
+        gz, gp = native_backward(ctx.mod, z, mask, params, planes, grad_out)
+        return (None, gz, None, *gp)

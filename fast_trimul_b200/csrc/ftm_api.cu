@@ -221,6 +221,17 @@ bool make_operand_map(CUtensorMap* m, const void* base, int L, int rows, int rpb
   return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, base, dims, strides, box);
 }
 
+// MN-major operand map: (row, k, l, 1, 1) with rows contiguous and k rows `rs` apart;
+// 64 x 64 boxes (two per 128-row half).
+bool make_operand_map_mn(CUtensorMap* m, const void* base, int L, int rows, int k, long long ls,
+                         long long rs) {
+  const uint64_t dims[5] = {uint64_t(rows), uint64_t(k), uint64_t(L), 1, 1};
+  const uint64_t strides[4] = {uint64_t(rs) * 2, uint64_t(ls) * 2, uint64_t(ls) * 2 * L,
+                               uint64_t(ls) * 2 * L};
+  const uint32_t box[5] = {64u, uint32_t(kCtBK), 1, 1, 1};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, base, dims, strides, box);
+}
+
 // Checks of a general layout (see ftm_contraction_layout); normalises single-block
 // sizes. Returns an ftm_status.
 int check_layout(ftm_contraction_layout* d) {
@@ -244,7 +255,15 @@ int check_layout(ftm_contraction_layout* d) {
                            d->b_kblock_stride, d->x_block_stride};
   for (long long s : opt)
     if (s < 0 || s % 8 != 0) return FTM_BAD_ALIGN;
-  if (d->a_row_stride < d->k_per_block || d->b_row_stride < d->k_per_block) return FTM_BAD_SHAPE;
+  if (d->a_mn_major || d->b_mn_major) {
+    // MN-major operands: one row block, one k block, rows contiguous
+    if (d->k_per_block != d->k) return FTM_BAD_SHAPE;
+    if (d->a_mn_major && (d->a_rows_per_block != d->m || d->a_row_stride < d->m)) return FTM_BAD_SHAPE;
+    if (d->b_mn_major && (d->b_rows_per_block != d->n || d->b_row_stride < d->n)) return FTM_BAD_SHAPE;
+  }
+  if ((!d->a_mn_major && d->a_row_stride < d->k_per_block) ||
+      (!d->b_mn_major && d->b_row_stride < d->k_per_block))
+    return FTM_BAD_SHAPE;
   if (!aligned16(d->a) || !aligned16(d->b) || !aligned16(d->x)) return FTM_BAD_ALIGN;
   return FTM_OK;
 }
@@ -252,15 +271,22 @@ int check_layout(ftm_contraction_layout* d) {
 int stage_contract_general(const ftm_contraction_layout& d, int* err, cudaStream_t stream, int dev,
                            const XDest* xdest = nullptr) {
   CUtensorMap amap, bmap;
-  if (!make_operand_map(&amap, d.a, d.L, d.m, d.a_rows_per_block, d.k, d.k_per_block,
-                        d.a_block_stride, d.a_l_stride, d.a_row_stride, d.a_kblock_stride) ||
-      !make_operand_map(&bmap, d.b, d.L, d.n, d.b_rows_per_block, d.k, d.k_per_block,
-                        d.b_block_stride, d.b_l_stride, d.b_row_stride, d.b_kblock_stride))
-    return FTM_LAUNCH_FAILED;
+  const bool a_ok = d.a_mn_major
+                        ? make_operand_map_mn(&amap, d.a, d.L, d.m, d.k, d.a_l_stride, d.a_row_stride)
+                        : make_operand_map(&amap, d.a, d.L, d.m, d.a_rows_per_block, d.k, d.k_per_block,
+                                           d.a_block_stride, d.a_l_stride, d.a_row_stride,
+                                           d.a_kblock_stride);
+  const bool b_ok = d.b_mn_major
+                        ? make_operand_map_mn(&bmap, d.b, d.L, d.n, d.k, d.b_l_stride, d.b_row_stride)
+                        : make_operand_map(&bmap, d.b, d.L, d.n, d.b_rows_per_block, d.k, d.k_per_block,
+                                           d.b_block_stride, d.b_l_stride, d.b_row_stride,
+                                           d.b_kblock_stride);
+  if (!a_ok || !b_ok) return FTM_LAUNCH_FAILED;
   CtLayout lay{d.a_rows_per_block, d.b_rows_per_block, d.k_per_block, d.x_rows_per_block,
                d.x_block_stride, d.x_l_stride, d.x_row_stride};
   const cudaError_t e = launch_contraction_pair(amap, bmap, static_cast<__half*>(d.x), d.L, d.m,
-                                                d.n, d.k, lay, err, sm_count(dev), stream, xdest);
+                                                d.n, d.k, lay, err, sm_count(dev), stream, xdest,
+                                                d.a_mn_major ? 1 : 0, d.b_mn_major ? 1 : 0);
   return e == cudaSuccess ? FTM_OK : FTM_LAUNCH_FAILED;
 }
 

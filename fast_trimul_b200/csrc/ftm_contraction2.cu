@@ -98,7 +98,10 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cl) {
                : "memory");
 }
 
-template <int NH>
+// AMN / BMN: operand A / B is MN-major (its rows contiguous in memory, k strided), loaded
+// as two 64-row swizzled atoms per 128-row half; the backward's transposed products
+// (dA = dX B, dB = dX^T A) read their operands this way without a transpose pass.
+template <int NH, int AMN = 0, int BMN = 0>
 __global__ void __launch_bounds__(kThreads, 1)
 contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
                         const __grid_constant__ CUtensorMap bmap, __half* __restrict__ X, int L,
@@ -192,10 +195,23 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
           const int kg = kb * kBK;
           const int kblk = kg / lay.k_rpb;
           const int kc = kg - kblk * lay.k_rpb;
-          tma_load_5d_pair(&amap, fb, sa, kc, ail, l, ablk, kblk);
+          if (AMN) {
+            tma_load_5d_pair(&amap, fb, sa, i0, kg, l, 0, 0);
+            tma_load_5d_pair(&amap, fb, sa + kATile / 2, i0 + 64, kg, l, 0, 0);
+          } else {
+            tma_load_5d_pair(&amap, fb, sa, kc, ail, l, ablk, kblk);
+          }
 #pragma unroll
-          for (int h = 0; h < NH; ++h)
-            tma_load_5d_pair(&bmap, fb, sa + kATile + h * kBTile, kc, bjl[h], l, bblk[h], kblk);
+          for (int h = 0; h < NH; ++h) {
+            uint8_t* sb = sa + kATile + h * kBTile;
+            if (BMN) {
+              const int j0 = (tn * NH + h) * 2 * kBN + static_cast<int>(rank) * kBN;
+              tma_load_5d_pair(&bmap, fb, sb, j0, kg, l, 0, 0);
+              tma_load_5d_pair(&bmap, fb, sb + kBTile / 2, j0 + 64, kg, l, 0, 0);
+            } else {
+              tma_load_5d_pair(&bmap, fb, sb, kc, bjl[h], l, bblk[h], kblk);
+            }
+          }
           ++issued;
           if (++st == kStages) {
             st = 0;
@@ -212,7 +228,7 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
   } else if (warp == 1) {
     if (leader && lane == 0) {
       // ------------------------------------------------ pair MMA issuer (leader)
-      constexpr uint32_t idesc = idesc_f16(0, 2 * kBM, 2 * kBN, 0, 0);
+      constexpr uint32_t idesc = idesc_f16(0, 2 * kBM, 2 * kBN, AMN, BMN);
       const uint32_t base = smem_u32(smem);
       int st = 0;
       uint32_t ph = 0;
@@ -236,10 +252,13 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
           const uint32_t sa = base + st * kStageBytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = kmajor_desc(sa + kk * 32);
+            // K-major: 16 k = 32 bytes along a swizzled row; MN-major: 16 k = 16 rows of
+            // two 64-element atoms 8 KB apart
+            const uint64_t ad = AMN ? sw128_desc(sa + kk * 2048, kATile / 2, 1024) : kmajor_desc(sa + kk * 32);
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
-              const uint64_t bd = kmajor_desc(sa + kATile + h * kBTile + kk * 32);
+              const uint32_t sb = sa + kATile + h * kBTile;
+              const uint64_t bd = BMN ? sw128_desc(sb + kk * 2048, kBTile / 2, 1024) : kmajor_desc(sb + kk * 32);
               umma_f16_pair(d + h * 256, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
             }
           }
@@ -335,7 +354,8 @@ contraction_pair_kernel(const __grid_constant__ CUtensorMap amap,
 
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
                                     int L, int M, int N, int K, const CtLayout& lay, int* err,
-                                    int num_sms, cudaStream_t stream, const XDest* xdest) {
+                                    int num_sms, cudaStream_t stream, const XDest* xdest,
+                                    int a_mn, int b_mn) {
   XDest xd{};
   if (xdest) xd = *xdest;
   // FTM_CT_NH=2 selects the 256 x 512 tile variant
@@ -354,6 +374,11 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
     return launch_pdl(kern, dim3(2 * clusters), dim3(kThreads), smem_bytes, stream, attr, 1, amap,
                       bmap, X, L, M, N, K, lay, err, xd);
   };
+  if (a_mn || b_mn) {
+    if (a_mn && b_mn) return go(contraction_pair_kernel<1, 1, 1>, PairCfg<1>::kSmemBytes, 256);
+    if (a_mn) return go(contraction_pair_kernel<1, 1, 0>, PairCfg<1>::kSmemBytes, 256);
+    return go(contraction_pair_kernel<1, 0, 1>, PairCfg<1>::kSmemBytes, 256);
+  }
   if (nh == 2) return go(contraction_pair_kernel<2>, PairCfg<2>::kSmemBytes, 512);
   return go(contraction_pair_kernel<1>, PairCfg<1>::kSmemBytes, 256);
 }

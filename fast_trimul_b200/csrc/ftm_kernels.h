@@ -114,7 +114,7 @@ struct CtLayout {
 cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X,
                                     int L, int M, int N, int K, const CtLayout& lay, int* err,
                                     int num_sms, cudaStream_t stream,
-                                    const XDest* xdest = nullptr);
+                                    const XDest* xdest = nullptr, int a_mn = 0, int b_mn = 0);
 
 cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap,
                                 const CUtensorMap& wmap, const CUtensorMap& omap,

@@ -145,6 +145,10 @@ int ftm_contraction_kblocked(const void* A, const void* B, void* X, int32_t L, i
  * aligned pointers; strides multiples of 8 elements (block strides may be 0 when there is
  * one block); n % 8 == 0; several row blocks need rows_per_block % 128 == 0 and the extent
  * a multiple of it; several k blocks need k_per_block % 64 == 0 and k a multiple of it.
+ * With a_mn_major = 1, A is stored with its rows contiguous instead:
+ *   A[l][i][kk] = a[l * a_l_stride + kk * a_row_stride + i]
+ * (one row block, one k block; a_row_stride >= m); b_mn_major likewise for B. The
+ * backward's products dA = dX B and dB = dX^T A read their operands this way.
  * Same reference code as ftm_contraction (_kernels.py:131-162). */
 typedef struct {
   int32_t L, m, n, k;
@@ -158,6 +162,7 @@ typedef struct {
   void* x;
   int32_t x_rows_per_block;
   int64_t x_block_stride, x_l_stride, x_row_stride;
+  int32_t a_mn_major, b_mn_major;
 } ftm_contraction_layout;
 int ftm_contraction_general(const ftm_contraction_layout* layout, int* err_word,
                             ftm_stream_t stream);

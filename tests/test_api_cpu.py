@@ -387,3 +387,42 @@ def test_parity_rows_checker_matches_oracle(mode, residual):
     got = reference_rows(m._impl, z, mask, rows, chunk_rows=7)
     ref = oracle_out(m, z, mask)[:, rows]
     assert np.abs(got.numpy() - ref).max() < 1e-4
+
+
+@pytest.mark.parametrize("mode", ["outgoing", "incoming"])
+def test_backward_plane_layout_on_cpu(mode, monkeypatch):
+    """The training backward (fast_trimul_b200.backward) with its native product swapped
+    for torch.bmm on the same planes: the gradients of z and of all parameters equal
+    autograd of the reference formula -- this pins the plane layouts of both modes."""
+    import torch.nn.functional as F
+    from fast_trimul_b200 import backward as bw
+    from tests.helpers import make_layer, make_mask
+
+    def torch_grads(dx, a, b):
+        return torch.bmm(dx, b.float()), torch.bmm(dx.transpose(1, 2), a.float())
+
+    monkeypatch.setattr(bw, "native_plane_grads", torch_grads)
+    m = make_layer(mode, True, d=16)
+    imp = m._impl.float()
+    gen = torch.Generator().manual_seed(6)
+    B, N, C = 2, 8, 16
+    z = torch.randn(B, N, N, C, generator=gen)
+    mask = make_mask("pad", B, N, gen)
+    gout = torch.randn(B, N, N, C, generator=gen)
+    params = [p.detach() for p in imp._params()]
+    # the forward's planes, as the native forward would keep them
+    with torch.no_grad():
+        mm = mask.unsqueeze(-1)
+        zn = F.layer_norm(z * mm, (C,), params[0], params[1], 1e-5)
+        a = F.linear(zn, params[4], params[5]) * torch.sigmoid(F.linear(zn, params[6], params[7]))
+        b = F.linear(zn, params[8], params[9]) * torch.sigmoid(F.linear(zn, params[10], params[11]))
+        a16 = bw._planes(a, mode).contiguous()
+        b16 = bw._planes(b, mode).contiguous()
+        x16 = torch.matmul(a16, b16.transpose(-1, -2))
+    gz, gp = bw.backward(imp, z, mask, params, (a16, b16, x16), gout)
+    zr = z.clone().requires_grad_(True)
+    pr = [p.clone().requires_grad_(True) for p in params]
+    out = imp._torch_forward(zr * mm, pr) * mm
+    want = torch.autograd.grad(out, [zr] + pr, gout)
+    for g, w in zip([gz] + gp, want):
+        assert torch.allclose(g, w, atol=1e-4, rtol=1e-3), (g - w).abs().max()

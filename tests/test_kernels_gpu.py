@@ -299,6 +299,48 @@ def test_contraction_general_strided(case):
 
 
 @needs_gpu
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("L,m,n,k", [(3, 256, 256, 320), (2, 384, 128, 512), (1, 200, 136, 72)])
+def test_contraction_mn_major_operands(a_mn, b_mn, L, m, n, k):
+    """MN-major A and/or B (rows contiguous, k strided): the operand forms of the
+    backward's dA = dX B and dB = dX^T A, against an fp32 matmul."""
+    import ctypes
+    from fast_trimul_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(14)
+    mp, np_ = (m + 7) // 8 * 8, (n + 7) // 8 * 8            # padded contiguous extents
+    A = torch.randn(L, m, k, device="cuda", generator=g).half()
+    B = torch.randn(L, n, k, device="cuda", generator=g).half()
+    d = _lib.ContractionLayout()
+    d.L, d.m, d.n, d.k, d.k_per_block = L, m, n, k, 0
+    if a_mn:
+        As = torch.zeros(L, k, mp, device="cuda", dtype=torch.half)
+        As[:, :, :m] = A.transpose(1, 2)
+        d.a, d.a_mn_major, d.a_l_stride, d.a_row_stride = As.data_ptr(), 1, k * mp, mp
+    else:
+        As = A.contiguous()
+        d.a, d.a_l_stride, d.a_row_stride = As.data_ptr(), m * k, k
+    if b_mn:
+        Bs = torch.zeros(L, k, np_, device="cuda", dtype=torch.half)
+        Bs[:, :, :n] = B.transpose(1, 2)
+        d.b, d.b_mn_major, d.b_l_stride, d.b_row_stride = Bs.data_ptr(), 1, k * np_, np_
+    else:
+        Bs = B.contiguous()
+        d.b, d.b_l_stride, d.b_row_stride = Bs.data_ptr(), n * k, k
+    X = torch.full((L, m, n), float("nan"), device="cuda", dtype=torch.half)
+    d.x, d.x_l_stride, d.x_row_stride = X.data_ptr(), m * n, n
+    err = torch.zeros(64, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    st = lib.ftm_contraction_general(ctypes.byref(d), err.data_ptr(), s)
+    assert st == 0, _lib.status_string(st)
+    assert lib.ftm_check_error(err.data_ptr(), None, s) == 0
+    ref = torch.bmm(A.float(), B.float().transpose(1, 2))
+    assert torch.isfinite(X).all()
+    rel = ((X.float() - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 2e-3, rel
+
+
+@needs_gpu
 def test_input_stage_incoming_row_shard():
     """Incoming mode on a non-square row shard (rows != cols): the transposed planes
     [c][i][k] of this shard's rows k, against the torch stand-in of the same stage."""

@@ -377,7 +377,48 @@ def bench_single(args, torch):
     res["e2e"] = bench_e2e(args, torch, layer, dev, n)
     res["sweep"] = bench_sweep(args, torch, layer, dev) if not args.no_sweep else None
     res["trunk"] = bench_trunk(args, torch, dev) if not args.no_trunk else None
+    res["train"] = bench_train(torch, dev) if not args.no_trunk else None
     return res
+
+
+def bench_train(torch, dev, ns=(384, 1024)):
+    """Forward + backward of one outgoing layer (B=1, bf16 z, all-ones mask, loss =
+    sum(out * g) for a fixed random g): this library's training path (native forward
+    keeping a, b, x; contraction gradients on the native kernel; per-position parts in
+    fp32 autograd) against the same layer run through the torch backend (the reference's
+    `_torch_forward` under autograd, fp16 weights). Median of 5 CUDA-event timed steps."""
+    from fast_trimul_b200 import FastTriangleMultiplication
+    rows = []
+    for n in ns:
+        for backend in ("cuda", "torch"):
+            torch.manual_seed(0)
+            layer = FastTriangleMultiplication(C, C, mode="outgoing", backend=backend).to(dev)
+            z = torch.randn(1, n, n, C, device=dev).to(torch.bfloat16).requires_grad_(True)
+            mask = torch.ones(1, n, n, device=dev)
+            g = torch.randn(1, n, n, C, device=dev)
+
+            def step():
+                out = layer(z, mask=mask)
+                (out.float() * g).sum().backward()
+
+            try:
+                for _ in range(2):
+                    step()
+                torch.cuda.synchronize()
+                ts = []
+                for _ in range(5):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    step()
+                    b.record()
+                    torch.cuda.synchronize()
+                    ts.append(a.elapsed_time(b))
+                rows.append({"n": n, "path": backend, "fwd_bwd_ms": round(statistics.median(ts), 3)})
+            except torch.cuda.OutOfMemoryError:
+                rows.append({"n": n, "path": backend, "fwd_bwd_ms": None, "note": "out of memory"})
+            del layer, z, g
+            torch.cuda.empty_cache()
+    return rows
 
 
 PARITY_ROWS = 16
@@ -832,6 +873,8 @@ def build_line(args, res, world):
         line["sweep"] = res["sweep"]
     if res.get("trunk"):
         line["trunk"] = res["trunk"]
+    if res.get("train"):
+        line["train"] = res["train"]
     if res.get("comm"):
         line["comm"] = res["comm"]
     if res.get("trace"):

@@ -10,7 +10,9 @@ Here the forward is the three native kernels, and it keeps the fp16 channel-majo
 planes a, b (the contraction's operands) and x (its result). The backward then
 
 * recomputes only the per-position parts (input LayerNorm, the four projections and
-  gates, the output LayerNorm, projection and gate) in fp32 with torch autograd;
+  gates, the output LayerNorm, projection and gate) with torch autograd, in the
+  weights' dtype (fp16 for the module, like the reference's backward; fp32 weights give
+  an fp32 recompute);
 * takes x from the forward instead of recomputing the contraction;
 * computes the contraction's gradients natively, on the tcgen05 contraction kernel
   with MN-major operands (no transpose pass) --
@@ -41,14 +43,15 @@ def _planes(t, mode):
 def native_plane_grads(dx_plane, a_plane, b_plane):
     """dA = dX B and dB = dX^T A per channel plane on the native kernel.
 
-    dx_plane: (L, N, N) fp32 gradient of X[l][i][j]; a_plane, b_plane: (L, N, N) fp16
-    contiguous operands of the forward (A[l][i][k], B[l][j][k]). Returns fp32 (dA, dB)."""
+    dx_plane: (L, N, N) gradient of X[l][i][j]; a_plane, b_plane: (L, N, N) fp16
+    contiguous operands of the forward (A[l][i][k], B[l][j][k]). Returns (dA, dB) in
+    dx_plane's dtype."""
     lib = _lib.load()
     L, N, _ = dx_plane.shape
-    scale = dx_plane.abs().amax()
+    scale = dx_plane.abs().amax().float()
     if scale.item() == 0.0:
         return torch.zeros_like(dx_plane), torch.zeros_like(dx_plane)
-    dx16 = (dx_plane / scale).to(torch.float16).contiguous()
+    dx16 = (dx_plane.float() / scale).to(torch.float16).contiguous()
     dA = torch.empty(L, N, N, dtype=torch.float16, device=dx_plane.device)
     dB = torch.empty_like(dA)
     err = _lib_err(dx_plane.device)
@@ -61,7 +64,7 @@ def native_plane_grads(dx_plane, a_plane, b_plane):
         d.x, d.x_l_stride, d.x_row_stride = out.data_ptr(), N * N, N
         _lib.check(lib.ftm_contraction_general(ctypes.byref(d), err, s), "ftm_contraction_general")
         _lib.stats["kernel_launches"] += 1
-    return dA.float() * scale, dB.float() * scale
+    return (dA.float() * scale).to(dx_plane.dtype), (dB.float() * scale).to(dx_plane.dtype)
 
 
 def _lib_err(device):
@@ -75,7 +78,7 @@ class _SavedContraction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, a_pl, b_pl, x16, a16, b16):
         ctx.save_for_backward(a16, b16)
-        return x16.float()
+        return x16.to(a_pl.dtype)
 
     @staticmethod
     def backward(ctx, dx):
@@ -92,10 +95,13 @@ def backward(mod, z, mask, params, planes, grad_out):
     planes: (a16, b16, x16), the forward's fp16 channel-major planes (B, C, N, N)."""
     a16, b16, x16 = planes
     eps_in, eps_out = mod.norm_in.eps, mod.norm_out.eps
+    # the per-position parts run in the weights' dtype (fp16 for the module, as the
+    # reference's own backward does), fp32 when the weights are fp32
+    ct = params[0].dtype if params[0].dtype in (torch.float16, torch.bfloat16) else torch.float32
     with torch.enable_grad():
-        zq = z.detach().float().requires_grad_(True)
-        p = [t.detach().float().requires_grad_(True) for t in params]
-        m = None if mask is None else mask.to(torch.float32).expand(z.shape[:3]).unsqueeze(-1)
+        zq = z.detach().to(ct).requires_grad_(True)
+        p = [t.detach().to(ct).requires_grad_(True) for t in params]
+        m = None if mask is None else mask.to(ct).expand(z.shape[:3]).unsqueeze(-1)
         zm = zq if m is None else zq * m
         zn = F.layer_norm(zm, (zm.shape[-1],), p[0], p[1], eps_in)
         a = F.linear(zn, p[4], p[5]) * torch.sigmoid(F.linear(zn, p[6], p[7]))
@@ -107,7 +113,7 @@ def backward(mod, z, mask, params, planes, grad_out):
         out = zm + delta if mod.residual else delta
         if m is not None:
             out = out * m
-    grads = torch.autograd.grad(out, [zq] + p, grad_out.to(torch.float32), allow_unused=True)
+    grads = torch.autograd.grad(out, [zq] + p, grad_out.to(ct), allow_unused=True)
     gz = grads[0].to(z.dtype)
     gp = [g.to(t.dtype) if g is not None else None for g, t in zip(grads[1:], params)]
     return gz, gp

@@ -46,8 +46,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu
 # capture of each kernel of this build at N=2048, B=1, outgoing.
-NCU_TRAFFIC_N2048 = {"contraction": 3789000000, "input_stage": 3181000000,
-                     "output_stage": 3204000000}
+NCU_TRAFFIC_N2048 = {"contraction": 4623865344, "input_stage": 3242864384,
+                     "output_stage": 3234792960}
 
 
 def trimul_flops(batch, n, c_z=C, c_h=C):

@@ -11,7 +11,8 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libfast_trimul_b200.so")
+# FTM_LIBRARY names another build of the same library (A/B measurements of two builds)
+LIB_PATH = os.environ.get("FTM_LIBRARY") or os.path.join(HERE, "libfast_trimul_b200.so")
 
 # status codes (ftm_status)
 OK, BAD_SHAPE, BAD_DTYPE, BAD_ALIGN, UNSUPPORTED_ARCH, LAUNCH_FAILED, TIMEOUT, BAD_WORKSPACE, \

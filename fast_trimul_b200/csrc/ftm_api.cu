@@ -3,6 +3,9 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <unordered_map>
+#include <utility>
 
 #include "../../include/fast_trimul_b200.h"
 #include "ftm_kernels.h"
@@ -62,11 +65,52 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // tiled map over `rank` dims (128B swizzle unless told otherwise); strides in bytes
 // for dims 1..rank-1
+// Encoding a tensor map costs microseconds of host time and a forward needs up to ~50 of
+// them; identical requests (same device, base, shape, strides, box) are served from a
+// bounded cache. A map holds no device state beyond the address it describes.
+struct MapKey {
+  int dev, dt, rank, swz;
+  const void* base;
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(&k);
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < sizeof(MapKey); ++i) h = (h ^ p[i]) * 1099511628211ull;
+    return static_cast<size_t>(h);
+  }
+};
+
 bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base,
               const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
               CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
+  MapKey key;
+  std::memset(&key, 0, sizeof(key));
+  if (cudaGetDevice(&key.dev) != cudaSuccess) return false;
+  key.dt = static_cast<int>(dt);
+  key.rank = rank;
+  key.swz = static_cast<int>(swz);
+  key.base = base;
+  for (int i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) key.strides[i] = strides[i];
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *m = it->second;
+      return true;
+    }
+  }
   cuuint64_t d[5], s[4];
   cuuint32_t b[5], e[5];
   for (int i = 0; i < rank; ++i) {
@@ -79,7 +123,11 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base
       fn(m, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
          CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() >= 1024) cache.clear();
+  cache.emplace(key, *m);
+  return true;
 }
 
 CUtensorMapDataType tma_dtype(int dt) {
@@ -429,6 +477,19 @@ WsLayout ws_layout(const ftm_problem* p) {
 }  // namespace
 
 namespace ftm {
+
+cudaError_t set_smem_once(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kern, dev})) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({kern, dev});
+  return e;
+}
 
 bool pdl_enabled() {
   const char* v = getenv("FTM_PDL");

@@ -201,8 +201,7 @@ size_t contraction_smem_bytes() { return kSmemBytes; }
 cudaError_t launch_contraction(const CUtensorMap& amap, const CUtensorMap& bmap, __half* X, int L,
                                int M, int N, int K, int rows_per_block, int* err, int grid,
                                cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(contraction_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = set_smem_once(reinterpret_cast<const void*>(contraction_kernel), kSmemBytes);
   if (e != cudaSuccess) return e;
   contraction_kernel<<<grid, kCtThreads, kSmemBytes, stream>>>(amap, bmap, X, L, M, N, K,
                                                                rows_per_block, err);

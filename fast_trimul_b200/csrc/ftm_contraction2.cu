@@ -362,7 +362,7 @@ cudaError_t launch_contraction_pair(const CUtensorMap& amap, const CUtensorMap& 
   const char* nh_env = getenv("FTM_CT_NH");
   const int nh = (nh_env && atoi(nh_env) == 2) ? 2 : 1;
   auto go = [&](auto kern, int smem_bytes, int tile_n) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    cudaError_t e = set_smem_once(reinterpret_cast<const void*>(kern), smem_bytes);
     if (e != cudaSuccess) return e;
     const long tiles = long(L) * ((M + 255) / 256) * ((N + tile_n - 1) / tile_n);
     const int clusters = static_cast<int>(tiles < num_sms / 2 ? tiles : num_sms / 2);

@@ -344,8 +344,7 @@ cudaError_t launch_input_stage(const CUtensorMap& zmap, const CUtensorMap& wmap,
                                const float* u_in, const float* v_in, float2* zstats,
                                const PosTiling& tl, int incoming, int z_bf16, float eps, int* err,
                                int grid, cudaStream_t stream, int test_stall) {
-  cudaError_t e = cudaFuncSetAttribute(input_stage_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = set_smem_once(reinterpret_cast<const void*>(input_stage_kernel), kSmemBytes);
   if (e != cudaSuccess) return e;
   return launch_pdl(input_stage_kernel, dim3(grid), dim3(kInThreads), kSmemBytes, stream, nullptr, 0,
                     zmap, wmap, smaps, mask, u_in, v_in, zstats, tl, incoming, z_bf16, eps, err,

@@ -14,6 +14,8 @@ namespace ftm {
 // set-up overlaps the tail of the previous kernel on the stream; the kernels call
 // grid_dep_wait() before their first global access.
 bool pdl_enabled();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel and device
+cudaError_t set_smem_once(const void* kern, int bytes);
 template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        const cudaLaunchAttribute* extra, int n_extra, Args... args) {

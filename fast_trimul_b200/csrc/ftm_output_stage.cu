@@ -443,7 +443,7 @@ cudaError_t launch_output_stage(const CUtensorMap& zmap, const CUtensorMap& xmap
                                 cudaStream_t stream) {
   auto go = [&](auto kern) -> cudaError_t {
     cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        set_smem_once(reinterpret_cast<const void*>(kern), kSmemBytes);
     if (e != cudaSuccess) return e;
     return launch_pdl(kern, dim3(grid), dim3(kOutThreads), kSmemBytes, stream, nullptr, 0, zmap, xmap,
                       wmap, omap, mask, zstats, u_g, v_g, u_o, v_o, out, tl, residual, z_bf16,

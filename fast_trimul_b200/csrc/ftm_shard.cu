@@ -26,6 +26,8 @@
 // Every wait is bounded (FTM_SHARD_WAIT_NS); an expired wait records
 // (KERNEL_EXCHANGE << 8) | (kind << 4) | 1 in the error word and lets the forward run on
 // (its output is then invalid; the caller reads the word with ftm_check_error).
+#include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -159,7 +161,30 @@ struct ftm_shard_plan {
   int push_ctas;
   unsigned int* push_done;  // counter for push_kernel (the plan's config scratch)
   PushList pending;         // runs queued for the next push
+  // FTM_SHARD_HOSTPROF=1: host time spent issuing each kind of work, printed at destroy
+  int hostprof;
+  double host_ns[8];
+  long long forwards;
 };
+
+namespace {
+enum { H_INPUT, H_CONTRACT, H_COPY, H_SIGNAL, H_WAIT, H_OUTPUT, H_TOTAL, H_COUNT };
+const char* const kHostNames[H_COUNT] = {"input stage", "contraction", "copies", "signals",
+                                         "waits", "output stage", "whole forward"};
+struct HostTimer {
+  ftm_shard_plan* pl;
+  int cat;
+  std::chrono::steady_clock::time_point t0;
+  HostTimer(ftm_shard_plan* p, int c) : pl(p), cat(c) {
+    if (pl->hostprof) t0 = std::chrono::steady_clock::now();
+  }
+  ~HostTimer() {
+    if (pl->hostprof)
+      pl->host_ns[cat] +=
+          std::chrono::duration<double, std::nano>(std::chrono::steady_clock::now() - t0).count();
+  }
+};
+}  // namespace
 
 namespace {
 
@@ -199,6 +224,7 @@ void mark(ftm_shard_plan* pl, cudaStream_t s, int what, int index) {
 }
 
 int wait_flags(ftm_shard_plan* pl, const FlagList& fl, int kind, cudaStream_t s) {
+  HostTimer ht(pl, H_WAIT);
   wait_flags_kernel<<<1, 32, 0, s>>>(pl->cfg.flags[pl->me], fl, pl->epoch, pl->cfg.err_word,
                                      (KERNEL_EXCHANGE << 8) | (kind << 4) | 1);
   ++pl->launches;
@@ -206,6 +232,7 @@ int wait_flags(ftm_shard_plan* pl, const FlagList& fl, int kind, cudaStream_t s)
 }
 
 int signal(ftm_shard_plan* pl, int q, int word) {
+  HostTimer ht(pl, H_SIGNAL);
   signal_kernel<<<1, 1, 0, pl->copy>>>(pl->cfg.flags[q] + word, pl->epoch);
   ++pl->launches;
   return fail(cudaGetLastError());
@@ -216,6 +243,7 @@ typedef unsigned short h16;   // fp16 element, for pointer arithmetic
 // Queue one run (bytes a multiple of 16) for the plan's push path: a copy-engine copy
 // right away, or a run of the next push_kernel launch.
 int push_run(ftm_shard_plan* pl, void* dst, const void* src, size_t bytes) {
+  HostTimer ht(pl, H_COPY);
   if (!pl->sm_push) return fail(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, pl->copy));
   PushList& p = pl->pending;
   if (p.count == kMaxSegs) return FTM_BAD_ARGUMENT;
@@ -287,6 +315,7 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
     }
     const h16* z_r = static_cast<const h16*>(z) + size_t(r) * rc * N * kC;
     const float* m_r = mask ? mask + size_t(r) * rc * N : nullptr;
+    HostTimer ht(pl, H_INPUT);
     if ((st = ftm_input_stage_scatter(&sub, z_r, m_r, c.packed, &pa, &pb,
                                       c.zstats + size_t(r) * rc * N * 2, c.err_word, cs)) != FTM_OK)
       return st;
@@ -345,7 +374,10 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
                  : static_cast<void*>(static_cast<h16*>(c.x_blocks) + size_t(o0) * owner_elems);
     d.x_rows_per_block = R; d.x_block_stride = owner_elems; d.x_l_stride = size_t(R) * N;
     d.x_row_stride = N;
-    if ((st = ftm_contraction_general(&d, c.err_word, cs)) != FTM_OK) return st;
+    {
+      HostTimer ht(pl, H_CONTRACT);
+      if ((st = ftm_contraction_general(&d, c.err_word, cs)) != FTM_OK) return st;
+    }
     ++pl->launches;
     mark(pl, cs, T_CONTRACT, g);
     if (direct) continue;
@@ -378,6 +410,7 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
   if (fx.count && (st = wait_flags(pl, fx, 2, cs)) != FTM_OK) return st;
   mark(pl, cs, T_X_READY, 0);
   ++pl->launches;
+  HostTimer ht(pl, H_OUTPUT);
   st = ftm_output_stage(&pl->out_problem, z, mask, c.x_plane[me], c.zstats, c.packed, out,
                         c.err_word, cs);
   mark(pl, cs, T_OUTPUT, 0);
@@ -519,6 +552,10 @@ int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
     // never written by peers)
     pl->push_done = reinterpret_cast<unsigned int*>(cfg->flags[cfg->rank] + FTM_SHARD_FLAG_WORDS - 1);
   }
+  {
+    const char* hp = getenv("FTM_SHARD_HOSTPROF");
+    pl->hostprof = (hp && strcmp(hp, "1") == 0) ? 1 : 0;
+  }
   bool ok = cudaStreamCreateWithFlags(&pl->copy, cudaStreamNonBlocking) == cudaSuccess;
   for (int i = 0; ok && i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
     ok = cudaEventCreateWithFlags(&pl->ev_in[i], cudaEventDisableTiming) == cudaSuccess;
@@ -553,8 +590,13 @@ int ftm_shard_forward(ftm_shard_plan* plan, const void* z, const float* mask, vo
   plan->launches = 0;
   plan->trace_n = 0;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  const int st = plan->cfg.scheme == FTM_SHARD_ALLTOALL ? forward_alltoall(plan, z, mask, out, cs)
-                                                         : forward_allgather(plan, z, mask, out, cs);
+  int st;
+  {
+    HostTimer ht(plan, H_TOTAL);
+    st = plan->cfg.scheme == FTM_SHARD_ALLTOALL ? forward_alltoall(plan, z, mask, out, cs)
+                                                : forward_allgather(plan, z, mask, out, cs);
+  }
+  ++plan->forwards;
   // the stage entry points set the per-thread count to 1 each; report the forward's total
   set_last_launch_count(st == FTM_OK ? plan->launches : 0);
   return st;
@@ -568,6 +610,13 @@ int ftm_shard_set_trace(ftm_shard_plan* plan, long long* trace) {
 
 void ftm_shard_plan_destroy(ftm_shard_plan* plan) {
   if (!plan) return;
+  if (plan->hostprof && plan->forwards) {
+    fprintf(stderr, "ftm_shard rank %d: host us per forward over %lld forwards:", plan->me,
+            plan->forwards);
+    for (int i = 0; i < H_COUNT; ++i)
+      fprintf(stderr, " %s %.1f;", kHostNames[i], plan->host_ns[i] / 1e3 / plan->forwards);
+    fprintf(stderr, "\n");
+  }
   if (plan->copy) cudaStreamSynchronize(plan->copy);
   for (int i = 0; i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
     if (plan->ev_in[i]) cudaEventDestroy(plan->ev_in[i]);

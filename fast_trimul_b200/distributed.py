@@ -903,10 +903,13 @@ def bench_sharded(args, torch_mod):
     dist.barrier()
     torch.cuda.synchronize()
     n_launch0 = _lib.stats["kernel_launches"]
+    import time
     with ClockSampler(local) as clk:
         t0.record()
+        h0 = time.perf_counter()
         for k in range(K):
             run(z, mask, out=out)
+        host_issue_ms = (time.perf_counter() - h0) * 1e3 / K
         t1.record()
         torch.cuda.synchronize()
     launches = _lib.stats["kernel_launches"] - n_launch0
@@ -960,7 +963,8 @@ def bench_sharded(args, torch_mod):
     stage_ms = _stages_alone(layer._impl, n, world, dev)
     res = None
     if rank == 0:
-        detail.update({"bytes_sent_per_rank_per_step": sh.comm_bytes_per_step(),
+        detail.update({"host_issue_ms_per_step": round(host_issue_ms, 3),
+                       "bytes_sent_per_rank_per_step": sh.comm_bytes_per_step(),
                        "nvlink_gbs_per_rank": round(sh.comm_bytes_per_step() / (ms.item() * 1e-3) / 1e9, 1)})
         res = {"ms_per_step": ms.item(), "rows_per_rank": hi - lo,
                "clocks": clocks, "gpu_launches": launches, "parity": parity,

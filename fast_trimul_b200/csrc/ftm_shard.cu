@@ -147,7 +147,10 @@ struct ftm_shard_plan {
   ftm_shard_config cfg;
   int P, me, RC, rc, R, N, B, L, lq, dev;
   size_t unit;              // fp16 elements of one channel of one chunk (rc * N)
-  cudaStream_t copy;        // copy-engine pushes and their signals
+  cudaStream_t copy;        // a/b pushes and their signals
+  cudaStream_t copy_x;      // x pushes and their signals: a forward's x pushes and the next
+                            // forward's a/b pushes must not queue behind each other
+  cudaStream_t cur;         // the one of the two the current pushes go to
   cudaEvent_t ev_in[FTM_SHARD_MAX_ROW_CHUNKS];
   cudaEvent_t ev_owner[FTM_MAX_RANKS];
   cudaEvent_t ev_pushed;    // last forward's a/b pushes done reading the local planes
@@ -159,7 +162,7 @@ struct ftm_shard_plan {
   ftm_problem out_problem;  // the shard problem with this forward's output dtype
   int sm_push;              // pushes by push_kernel (FTM_SHARD_PUSH=sm) instead of copy engines
   int push_ctas;
-  unsigned int* push_done;  // counter for push_kernel (the plan's config scratch)
+  unsigned int* push_done;  // counters for push_kernel, one per copy stream
   PushList pending;         // runs queued for the next push
   // FTM_SHARD_HOSTPROF=1: host time spent issuing each kind of work, printed at destroy
   int hostprof;
@@ -233,7 +236,7 @@ int wait_flags(ftm_shard_plan* pl, const FlagList& fl, int kind, cudaStream_t s)
 
 int signal(ftm_shard_plan* pl, int q, int word) {
   HostTimer ht(pl, H_SIGNAL);
-  signal_kernel<<<1, 1, 0, pl->copy>>>(pl->cfg.flags[q] + word, pl->epoch);
+  signal_kernel<<<1, 1, 0, pl->cur>>>(pl->cfg.flags[q] + word, pl->epoch);
   ++pl->launches;
   return fail(cudaGetLastError());
 }
@@ -244,7 +247,7 @@ typedef unsigned short h16;   // fp16 element, for pointer arithmetic
 // right away, or a run of the next push_kernel launch.
 int push_run(ftm_shard_plan* pl, void* dst, const void* src, size_t bytes) {
   HostTimer ht(pl, H_COPY);
-  if (!pl->sm_push) return fail(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, pl->copy));
+  if (!pl->sm_push) return fail(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, pl->cur));
   PushList& p = pl->pending;
   if (p.count == kMaxSegs) return FTM_BAD_ARGUMENT;
   p.src[p.count] = static_cast<const uint4*>(src);
@@ -272,9 +275,9 @@ int push_flush(ftm_shard_plan* pl, unsigned who, int word) {
   for (int q = 0; q < pl->P; ++q)
     if (who & (1u << q)) p.flag[p.nflags++] = pl->cfg.flags[q] + word;
   p.epoch = pl->epoch;
-  p.done = pl->push_done;
+  p.done = pl->push_done + (pl->cur == pl->copy ? 0 : 1);
   if (p.count || p.nflags) {
-    push_kernel<<<pl->push_ctas, 256, 0, pl->copy>>>(p);
+    push_kernel<<<pl->push_ctas, 256, 0, pl->cur>>>(p);
     ++pl->launches;
     if ((st = fail(cudaGetLastError())) != FTM_OK) return st;
   }
@@ -345,6 +348,7 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
   // the previous forward's x pushes must be done reading the x blocks
   if ((st = fail(cudaStreamWaitEvent(cs, pl->ev_x_pushed, 0))) != FTM_OK) return st;
 
+  pl->cur = pl->copy_x;
   // received: [slot][src s][chunk r][a | b][batch][lq][rc][N]
   const h16* Rs = static_cast<const h16*>(c.recv_a[me]) + size_t(slot) * slot_elems;
   const size_t owner_elems = size_t(B) * lq * R * N;
@@ -382,7 +386,7 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
     mark(pl, cs, T_CONTRACT, g);
     if (direct) continue;
     if ((st = fail(cudaEventRecord(pl->ev_owner[g], cs))) != FTM_OK) return st;
-    if ((st = fail(cudaStreamWaitEvent(pl->copy, pl->ev_owner[g], 0))) != FTM_OK) return st;
+    if ((st = fail(cudaStreamWaitEvent(pl->copy_x, pl->ev_owner[g], 0))) != FTM_OK) return st;
     for (int o = o0; o < o0 + G; ++o) {
       const h16* src = static_cast<const h16*>(c.x_blocks) + size_t(o) * owner_elems;
       h16* dst = static_cast<h16*>(c.x_plane[o]) + size_t(me) * lq * R * N;
@@ -391,11 +395,11 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
         if ((st = push_run(pl, dst + size_t(b) * kC * R * N, src + size_t(b) * lq * R * N,
                            size_t(lq) * R * N * 2)) != FTM_OK)
           return st;
-      if (!pl->sm_push) mark(pl, pl->copy, T_X_SENT, o);
+      if (!pl->sm_push) mark(pl, pl->copy_x, T_X_SENT, o);
     }
     if (pl->sm_push) {
       if ((st = push_flush(pl, 0u, 0)) != FTM_OK) return st;
-      mark(pl, pl->copy, T_X_SENT, g);
+      mark(pl, pl->copy_x, T_X_SENT, g);
     }
   }
   // owners wait for every source's x: one flag per owner, after the last push
@@ -403,7 +407,7 @@ int forward_alltoall(ftm_shard_plan* pl, const void* z, const float* mask, void*
   for (int o = 0; o < P; ++o)
     if (!(o == me && direct_own)) who |= 1u << o;
   if ((st = push_flush(pl, who, kFlagX + me)) != FTM_OK) return st;
-  if ((st = fail(cudaEventRecord(pl->ev_x_pushed, pl->copy))) != FTM_OK) return st;
+  if ((st = fail(cudaEventRecord(pl->ev_x_pushed, pl->copy_x))) != FTM_OK) return st;
   FlagList fx{};
   for (int s = 0; s < P; ++s)
     if (s != me || !direct_own) fx.idx[fx.count++] = kFlagX + s;
@@ -550,13 +554,14 @@ int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
     if (pl->push_ctas > 1024) pl->push_ctas = 1024;
     // the counter lives in the last word of this rank's flag buffer (zeroed by the caller,
     // never written by peers)
-    pl->push_done = reinterpret_cast<unsigned int*>(cfg->flags[cfg->rank] + FTM_SHARD_FLAG_WORDS - 1);
+    pl->push_done = reinterpret_cast<unsigned int*>(cfg->flags[cfg->rank] + FTM_SHARD_FLAG_WORDS - 2);
   }
   {
     const char* hp = getenv("FTM_SHARD_HOSTPROF");
     pl->hostprof = (hp && strcmp(hp, "1") == 0) ? 1 : 0;
   }
-  bool ok = cudaStreamCreateWithFlags(&pl->copy, cudaStreamNonBlocking) == cudaSuccess;
+  bool ok = cudaStreamCreateWithFlags(&pl->copy, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&pl->copy_x, cudaStreamNonBlocking) == cudaSuccess;
   for (int i = 0; ok && i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
     ok = cudaEventCreateWithFlags(&pl->ev_in[i], cudaEventDisableTiming) == cudaSuccess;
   for (int i = 0; ok && i < FTM_MAX_RANKS; ++i)
@@ -565,7 +570,7 @@ int ftm_shard_plan_create(const ftm_shard_config* cfg, ftm_shard_plan** plan) {
   ok = ok && cudaEventCreateWithFlags(&pl->ev_x_pushed, cudaEventDisableTiming) == cudaSuccess;
   // recorded once so the first forward's waits on them are satisfied
   ok = ok && cudaEventRecord(pl->ev_pushed, pl->copy) == cudaSuccess;
-  ok = ok && cudaEventRecord(pl->ev_x_pushed, pl->copy) == cudaSuccess;
+  ok = ok && cudaEventRecord(pl->ev_x_pushed, pl->copy_x) == cudaSuccess;
   if (!ok) {
     ftm_shard_plan_destroy(pl);
     return FTM_LAUNCH_FAILED;
@@ -589,6 +594,7 @@ int ftm_shard_forward(ftm_shard_plan* plan, const void* z, const float* mask, vo
   ++plan->epoch;
   plan->launches = 0;
   plan->trace_n = 0;
+  plan->cur = plan->copy;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   int st;
   {
@@ -618,6 +624,7 @@ void ftm_shard_plan_destroy(ftm_shard_plan* plan) {
     fprintf(stderr, "\n");
   }
   if (plan->copy) cudaStreamSynchronize(plan->copy);
+  if (plan->copy_x) cudaStreamSynchronize(plan->copy_x);
   for (int i = 0; i < FTM_SHARD_MAX_ROW_CHUNKS; ++i)
     if (plan->ev_in[i]) cudaEventDestroy(plan->ev_in[i]);
   for (int i = 0; i < FTM_MAX_RANKS; ++i)
@@ -625,6 +632,7 @@ void ftm_shard_plan_destroy(ftm_shard_plan* plan) {
   if (plan->ev_pushed) cudaEventDestroy(plan->ev_pushed);
   if (plan->ev_x_pushed) cudaEventDestroy(plan->ev_x_pushed);
   if (plan->copy) cudaStreamDestroy(plan->copy);
+  if (plan->copy_x) cudaStreamDestroy(plan->copy_x);
   delete plan;
 }
 

@@ -591,10 +591,12 @@ def default_pipeline_scheme(world, mode="outgoing"):
     return "p2p_allgather" if world == 2 and mode == "outgoing" else "p2p_alltoall"
 
 
-def default_row_chunks(rows, batch=1):
+def default_row_chunks(rows, batch=1, world=1):
     """Row chunks of the input stage: each chunk's exchange starts when it is done.
-    Chunks of at least 128 rows (the contraction's row / k blocks), at most 4."""
-    if batch > 1:
+    Chunks of at least 128 rows (the contraction's row / k blocks), at most 4. At 8
+    ranks one chunk: its pushes per peer are then 2x larger, which the copy engines
+    move faster (measured 610 vs 450 GB/s), and the input stage is short."""
+    if batch > 1 or world >= 8:
         return 1
     for rc in (4, 3, 2):
         if rows % rc == 0 and (rows // rc) % 128 == 0:
@@ -633,7 +635,7 @@ class ShardedTriMul:
         self.device = dev
         self.z_dtype = z_dtype
         self.out_dtype = z_dtype if out_dtype is None else out_dtype
-        self.row_chunks = row_chunks or default_row_chunks(self.rows, batch)
+        self.row_chunks = row_chunks or default_row_chunks(self.rows, batch, self.world)
         lib = _lib.load()
         self.lib = lib
         probe = torch.empty(batch, self.rows, n, C, dtype=z_dtype, device="meta")

@@ -378,8 +378,45 @@ def bench_single(args, torch):
     res["sweep"] = bench_sweep(args, torch, layer, dev) if not args.no_sweep else None
     res["trunk"] = bench_trunk(args, torch, dev) if not args.no_trunk else None
     res["train"] = bench_train(torch, dev) if not args.no_trunk else None
+    res["small_n"] = bench_small_n(torch, dev) if not args.no_sweep else None
     return res
 
+
+def bench_small_n(torch, dev, ns=(64, 128, 256)):
+    """Latency of one outgoing layer call through the public module API at small N
+    (B=1, bf16 z, ones mask): eager (`layer(z, mask)`: dispatch, a workspace from the
+    caching allocator, three launches) and after `layer.graphed(z, mask)` (replay of the
+    three launches, z already in the graph's input buffer). Median of 50 CUDA-event timed
+    calls each, back to back (z is small enough to stay in L2: this is a latency figure)."""
+    from fast_trimul_b200 import FastTriangleMultiplication
+    rows = []
+    for n in ns:
+        torch.manual_seed(0)
+        layer = FastTriangleMultiplication(C, C, mode="outgoing").to(dev).eval()
+        z = torch.randn(1, n, n, C, device=dev).to(torch.bfloat16)
+        mask = torch.ones(1, n, n, device=dev)
+
+        def timed(fn):
+            for _ in range(5):
+                fn()
+            ts = []
+            for _ in range(50):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+            return statistics.median(ts)
+
+        with torch.no_grad():
+            eager = timed(lambda: layer(z, mask=mask))
+            layer.graphed(z, mask)
+            zin = layer.graph_input()
+            graphed = timed(lambda: layer(zin, mask=mask))
+        rows.append({"n": n, "eager_ms": round(eager, 4), "graphed_ms": round(graphed, 4)})
+        del layer, z
+    return rows
 
 def bench_train(torch, dev, ns=(384, 1024)):
     """Forward + backward of one outgoing layer (B=1, bf16 z, all-ones mask, loss =
@@ -482,7 +519,7 @@ def contraction_alone(torch, n, reps=10):
             "note": "back-to-back launches; operands 0.54 GB > L2 is not guaranteed, L2 not flushed"}
 
 
-def reference_gpu_subprocess(ns=(256, 2048), timeout_s=300):
+def reference_gpu_subprocess(ns=(64, 128, 256, 2048), timeout_s=300):
     """Times the reference's own GPU kernels (its FastTriangleMultiplication with CUDA-graph
     capture, from baseline/_ref) on this GPU in a child process, so its JIT-compiled
     CuTe kernels cannot disturb this process. Returns a list of per-N results or an
@@ -881,7 +918,7 @@ def build_line(args, res, world):
         line["trace"] = res["trace"]
     if res.get("stage_note"):
         line["stages_note"] = res["stage_note"]
-    for key in ("parity", "contraction_n1024"):
+    for key in ("parity", "contraction_n1024", "small_n"):
         if res.get(key):
             line[key] = res[key]
     return line
@@ -960,6 +997,7 @@ def main():
         rg = reference_gpu_subprocess()
         if isinstance(rg, list):
             ours = {r["n"]: r["ms"] for r in (line.get("sweep") or []) if r["mode"] == "outgoing"}
+            ours.update({r["n"]: r["graphed_ms"] for r in (res.get("small_n") or [])})   # graphed vs graphed
             ours[args.n] = line["ms_per_step"]
             for r in rg:
                 if r.get("n") in ours and r.get("graphed_ms"):

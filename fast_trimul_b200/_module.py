@@ -249,10 +249,10 @@ class TriangleMultiplicativeUpdateKernelFused(nn.Module):
 
 
 class _TrainableTriMul(torch.autograd.Function):
-    """Native forward that keeps the planes a, b, x; backward with the contraction's
-    gradients on the native kernel and the per-position parts recomputed in fp32
-    (fast_trimul_b200.backward). Replaces the reference's recompute-everything
-    backward (_kernels.py:468-488)."""
+    """Native forward that keeps the planes a, b, x; native backward: the contraction's
+    gradients on the tcgen05 kernel, per-position GEMMs on cuBLAS, the elementwise and
+    LayerNorm parts in the ftm_bwd_* kernels (fast_trimul_b200.backward). Replaces the
+    reference's recompute-everything backward (_kernels.py:468-488)."""
 
     @staticmethod
     def forward(ctx, mod, z, mask, *params):
@@ -265,12 +265,17 @@ class _TrainableTriMul(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        from .backward import backward as native_backward
+        import os
+        from . import backward as bw
         saved = ctx.saved_tensors
         z = saved[0]
         mask = saved[1] if ctx.has_mask else None
         first = 2 if ctx.has_mask else 1
         params = list(saved[first:first + 16])
         planes = saved[first + 16:first + 19]
-        gz, gp = native_backward(ctx.mod, z, mask, params, planes, grad_out)
+        # FTM_BACKWARD=recompute: the per-position parts through torch autograd instead
+        if os.environ.get("FTM_BACKWARD") == "recompute":
+            gz, gp = bw.backward(ctx.mod, z, mask, params, planes, grad_out)
+        else:
+            gz, gp = bw.backward_native(ctx.mod, z, mask, params, planes, grad_out)
         return (None, gz, None, *gp)

@@ -18,7 +18,7 @@ PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "libfast_trimul_b200.so")
 SOURCES = ["ftm_api.cu", "ftm_pack.cu", "ftm_input_stage.cu", "ftm_contraction.cu", "ftm_contraction2.cu",
-           "ftm_output_stage.cu", "ftm_shard.cu", "ftm_noalloc.cu"]
+           "ftm_output_stage.cu", "ftm_shard.cu", "ftm_backward.cu", "ftm_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
           "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]

@@ -96,16 +96,21 @@ def test_gradients_are_finite():
 
 
 @needs_gpu
+@pytest.mark.parametrize("backward", ["native", "recompute"])
+@pytest.mark.parametrize("masked", [True, False])
 @pytest.mark.parametrize("mode", ["outgoing", "incoming"])
-def test_gradients_match_fp32_autograd(mode):
+def test_gradients_match_fp32_autograd(mode, masked, backward, monkeypatch):
     """Gradients of z and of all 16 parameters through the layer's training path match
     torch autograd of the fp32 module (the reference formula, _kernels.py:532-547, on
     fp32 copies of the same fp16 weights) with the same mask rules. Tolerance: the
     gradient's max-abs error relative to its largest entry, at fp16-storage level."""
-    import torch.nn.functional as F  # noqa: F401
+    if backward == "recompute":
+        monkeypatch.setenv("FTM_BACKWARD", "recompute")
     m = make_layer(mode, True).cuda()
     z, mask = _inputs(48, 37, dtype=torch.float32)
     z, mask = z.cuda(), mask.cuda()
+    if not masked:
+        mask = torch.ones_like(mask)
     g = torch.Generator(device="cuda").manual_seed(38)
     gout = torch.randn(z.shape, device="cuda", generator=g)
     zq = z.clone().requires_grad_(True)

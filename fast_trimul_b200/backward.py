@@ -214,13 +214,16 @@ def backward_native(mod, z, mask, params, planes, grad_out):
     O = xn @ W_o.t()
     dO = torch.empty(P, C, dtype=torch.float16, device=dev)
     dPGZ = torch.empty(P, 640, dtype=torch.float16, device=dev)
+    nb = lib.ftm_bwd_partial_blocks()
+    part_g = torch.empty(nb, 2 * C, dtype=torch.float32, device=dev)
     chk(lib.ftm_bwd_gate(O.data_ptr(), b_o.data_ptr(), H.data_ptr(), b_g.data_ptr(), gout.data_ptr(),
-                         _DT[gout.dtype], gsc, mp, dO.data_ptr(), dPGZ.data_ptr(), P, s), "ftm_bwd_gate")
+                         _DT[gout.dtype], gsc, mp, dO.data_ptr(), dPGZ.data_ptr(), part_g.data_ptr(),
+                         P, s), "ftm_bwd_gate")
     del O
     dxn = dO @ W_o
     dW_o = _mm32(dO.t(), xn)
-    db_o = dO.sum(0, dtype=torch.float32)
-    nb = lib.ftm_bwd_partial_blocks()
+    sg = part_g.sum(0)
+    db_o, db_gz = sg[:C], sg[C:]
     part = torch.empty(nb, 2 * C, dtype=torch.float32, device=dev)
     dxp = torch.empty(L, N, N, dtype=torch.float32, device=dev)
     chk(lib.ftm_bwd_x_ln_bwd(x16.data_ptr(), xst.data_ptr(), dxn.data_ptr(), g_out.data_ptr(),
@@ -230,12 +233,13 @@ def backward_native(mod, z, mask, params, planes, grad_out):
     del dxn, xn, dO
     dA, dB, dsc = native_plane_grads_pos(dxp, a16.reshape(L, N, N), b16.reshape(L, N, N), mod.mode)
     del dxp
+    part_in = torch.empty(nb, 4 * C, dtype=torch.float32, device=dev)
     chk(lib.ftm_bwd_gates_in(dA.data_ptr(), dB.data_ptr(), dsc, H.data_ptr(), b_in.data_ptr(),
-                             dPGZ.data_ptr(), B, N, s), "ftm_bwd_gates_in")
+                             dPGZ.data_ptr(), part_in.data_ptr(), B, N, s), "ftm_bwd_gates_in")
     del dA, dB, H
     dzn = dPGZ @ W_all                                          # (P, 128)
     dW_all = _mm32(dPGZ.t(), zn)                                # (640, 128)
-    db_all = dPGZ.sum(0, dtype=torch.float32)
+    db_all = torch.cat([part_in.sum(0), db_gz])
     del dPGZ, zn
     dz = torch.empty(z.shape, dtype=zc.dtype, device=dev)
     part2 = torch.empty(nb, 2 * C, dtype=torch.float32, device=dev)

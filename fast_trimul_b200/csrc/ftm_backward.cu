@@ -89,19 +89,47 @@ __global__ void ln_in_kernel(const void* __restrict__ z, int z_dtype, const floa
   }
 }
 
-// Plane tile (b, u, v0 .. v0 + 31) x 128 channels -> shared memory tile[c][j].
-template <typename T>
-__device__ __forceinline__ void load_plane_tile(const T* __restrict__ plane, int b, int u, int v0,
-                                                int N, float (*tile)[kTile + 1]) {
+// Plane tile (b, u, v0 .. v0 + 31) x 128 channels of an fp16 plane -> shared memory
+// tile[c][j], 8 positions (16 bytes) per load where the row allows it.
+__device__ __forceinline__ void load_plane_tile(const __half* __restrict__ plane, int b, int u,
+                                                int v0, int N, float (*tile)[kTile + 1]) {
+  const bool vec = (v0 + kTile <= N) && (N % 8 == 0);
+  if (vec) {
+    for (int idx = threadIdx.x; idx < kC * (kTile / 8); idx += blockDim.x) {
+      const int c = idx / (kTile / 8), j8 = (idx % (kTile / 8)) * 8;
+      const uint4 w = *reinterpret_cast<const uint4*>(
+          plane + ((static_cast<size_t>(b) * kC + c) * N + u) * N + v0 + j8);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ws[q]));
+        tile[c][j8 + 2 * q] = f.x;
+        tile[c][j8 + 2 * q + 1] = f.y;
+      }
+    }
+    return;
+  }
   for (int idx = threadIdx.x; idx < kC * kTile; idx += blockDim.x) {
     const int c = idx / kTile, j = idx % kTile, v = v0 + j;
-    float val = 0.f;
-    if (v < N) {
-      const T x = plane[((static_cast<size_t>(b) * kC + c) * N + u) * N + v];
-      if constexpr (sizeof(T) == 2) val = __half2float(x);
-      else val = x;
-    }
-    tile[c][j] = val;
+    tile[c][j] = v < N ? __half2float(plane[((static_cast<size_t>(b) * kC + c) * N + u) * N + v]) : 0.f;
+  }
+}
+
+// Block-wide sums of per-thread channel partials (four channels per lane, `groups` groups
+// of 128 channels) written as one row of `partial`.
+template <int G>
+__device__ __forceinline__ void write_partials(float (*red)[G * kC], const float (&acc)[G][4],
+                                               float* partial) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) red[warp][g * kC + 4 * lane + k] = acc[g][k];
+  __syncthreads();
+  for (int c = threadIdx.x; c < G * kC; c += blockDim.x) {
+    float s = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += red[w][c];
+    partial[static_cast<size_t>(blockIdx.x) * G * kC + c] = s;
   }
 }
 
@@ -151,7 +179,9 @@ __global__ void gate_bwd_kernel(const __half* __restrict__ O, const float* __res
                                 const __half* __restrict__ H, const float* __restrict__ b_g,
                                 const void* __restrict__ gout, int g_dtype, float g_scale,
                                 const float* __restrict__ mask, __half* __restrict__ dO,
-                                __half* __restrict__ dPGZ, long long P) {
+                                __half* __restrict__ dPGZ, float* __restrict__ partial, long long P) {
+  __shared__ float red[8][2 * kC];
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const float4 bo = *reinterpret_cast<const float4*>(b_o + 4 * lane);
@@ -171,10 +201,13 @@ __global__ void gate_bwd_kernel(const __half* __restrict__ O, const float* __res
       const float dd = g[k] * m;
       dov[k] = dd * s;
       dgz[k] = dd * (o[k] + bo_[k]) * s * (1.f - s);
+      acc[0][k] += dov[k];
+      acc[1][k] += dgz[k];
     }
     store4(dO, FTM_F16, static_cast<size_t>(p) * kC + 4 * lane, dov);
     store4(dPGZ, FTM_F16, static_cast<size_t>(p) * kH + 512 + 4 * lane, dgz);
   }
+  write_partials<2>(red, acc, partial);
 }
 
 // ---------------------------------------------------------------- output LayerNorm backward
@@ -246,9 +279,10 @@ __global__ void x_ln_bwd_kernel(const __half* __restrict__ xplane, const float2*
 __global__ void gates_in_bwd_kernel(const __half* __restrict__ dA, const __half* __restrict__ dB,
                                     float dscale, const __half* __restrict__ H,
                                     const float* __restrict__ b_in, __half* __restrict__ dPGZ,
-                                    int B, int N) {
+                                    float* __restrict__ partial, int B, int N) {
   __shared__ float ta[kC][kTile + 1];
   __shared__ float tb[kC][kTile + 1];
+  float acc[4][4] = {};
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int vt = (N + kTile - 1) / kTile;
   const long long tiles = static_cast<long long>(B) * N * vt;
@@ -281,12 +315,17 @@ __global__ void gates_in_bwd_kernel(const __half* __restrict__ dA, const __half*
           const float s = sigmoidf(gr[k] + bias[2 * half + 1][k]);
           dpv[k] = d * s;
           dgv[k] = d * pv * s * (1.f - s);
+          acc[2 * half][k] += dpv[k];
+          acc[2 * half + 1][k] += dgv[k];
         }
         store4(dPGZ, FTM_F16, p * kH + half * 256 + 4 * lane, dpv);
         store4(dPGZ, FTM_F16, p * kH + half * 256 + 128 + 4 * lane, dgv);
       }
     }
   }
+  __syncthreads();
+  // the tiles are free now: reuse them as the reduction buffer (8 warps x 512 floats)
+  write_partials<4>(reinterpret_cast<float (*)[4 * kC]>(&ta[0][0]), acc, partial);
 }
 
 // ---------------------------------------------------------------- input LayerNorm backward
@@ -388,12 +427,13 @@ int ftm_bwd_x_ln(const void* xplane, const float* gamma, const float* beta, floa
 
 int ftm_bwd_gate(const void* O, const float* b_o, const void* H, const float* b_g, const void* gout,
                  int32_t g_dtype, float g_scale, const float* mask, void* dO, void* dPGZ,
-                 int64_t positions, ftm_stream_t stream) {
-  if (!O || !b_o || !H || !b_g || !gout || !dO || !dPGZ || positions < 1 || !dtype_ok(g_dtype))
+                 float* partial, int64_t positions, ftm_stream_t stream) {
+  if (!O || !b_o || !H || !b_g || !gout || !dO || !dPGZ || !partial || positions < 1 ||
+      !dtype_ok(g_dtype))
     return FTM_BAD_ARGUMENT;
   gate_bwd_kernel<<<bwd_blocks(), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(O), b_o, static_cast<const __half*>(H), b_g, gout, g_dtype, g_scale,
-      mask, static_cast<__half*>(dO), static_cast<__half*>(dPGZ), positions);
+      mask, static_cast<__half*>(dO), static_cast<__half*>(dPGZ), partial, positions);
   return launched(cudaSuccess);
 }
 
@@ -408,11 +448,11 @@ int ftm_bwd_x_ln_bwd(const void* xplane, const float* stats, const void* dxn, co
 }
 
 int ftm_bwd_gates_in(const void* dA, const void* dB, float dscale, const void* H, const float* b_in,
-                     void* dPGZ, int32_t batch, int32_t n, ftm_stream_t stream) {
-  if (!dA || !dB || !H || !b_in || !dPGZ || batch < 1 || n < 1) return FTM_BAD_ARGUMENT;
+                     void* dPGZ, float* partial, int32_t batch, int32_t n, ftm_stream_t stream) {
+  if (!dA || !dB || !H || !b_in || !dPGZ || !partial || batch < 1 || n < 1) return FTM_BAD_ARGUMENT;
   gates_in_bwd_kernel<<<bwd_blocks(), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(dA), static_cast<const __half*>(dB), dscale,
-      static_cast<const __half*>(H), b_in, static_cast<__half*>(dPGZ), batch, n);
+      static_cast<const __half*>(H), b_in, static_cast<__half*>(dPGZ), partial, batch, n);
   return launched(cudaSuccess);
 }
 

@@ -938,6 +938,8 @@ def main():
                     help="reference arm: skip the one full-size CPU forward")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own GPU kernels (reference_gpu key)")
+    ap.add_argument("--trace-timed", action="store_true",
+                    help="N>1: keep the timeline markers on during the timed steps (diagnostic)")
     ap.add_argument("--trace", action="store_true",
                     help="N>1: add the device-clock timeline of one forward per rank (trace key)")
     ap.add_argument("--push", default=None, choices=["ce", "sm"],

@@ -51,7 +51,7 @@ class DeviceErrorWord:
         self.ptr = self.dev.data_ptr()
 
     def after_launch(self):
-        if torch.cuda.is_current_stream_capturing():
+        if torch.cuda.is_current_stream_capturing() or _NO_ASYNC_CHECK:
             return
         self.host.copy_(self.dev[:1], non_blocking=True)
         self.event = torch.cuda.Event()
@@ -83,6 +83,8 @@ class DeviceErrorWord:
 
 
 _ERROR_WORDS = {}
+# FTM_ERROR_POLL=0: no per-call copy of the word (errors then surface at check() only)
+_NO_ASYNC_CHECK = __import__("os").environ.get("FTM_ERROR_POLL") == "0"
 
 
 def device_error_word(device):

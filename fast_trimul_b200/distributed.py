@@ -906,14 +906,24 @@ def bench_sharded(args, torch_mod):
     torch.cuda.synchronize()
     n_launch0 = _lib.stats["kernel_launches"]
     import time
+    if getattr(args, "trace_timed", False) and hasattr(sh, "enable_trace"):
+        sh.enable_trace()
+    spans = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(K)]
     with ClockSampler(local) as clk:
         t0.record()
         h0 = time.perf_counter()
         for k in range(K):
+            spans[k][0].record()
             run(z, mask, out=out)
+            spans[k][1].record()
         host_issue_ms = (time.perf_counter() - h0) * 1e3 / K
         t1.record()
         torch.cuda.synchronize()
+    span_ms = sorted(a.elapsed_time(b) for a, b in spans)
+    gap_ms = sorted(spans[k][1].elapsed_time(spans[k + 1][0]) for k in range(K - 1))
+    if getattr(args, "trace_timed", False) and hasattr(sh, "disable_trace"):
+        sh.disable_trace()
     launches = _lib.stats["kernel_launches"] - n_launch0
     dist.barrier()
     check()
@@ -966,6 +976,8 @@ def bench_sharded(args, torch_mod):
     res = None
     if rank == 0:
         detail.update({"host_issue_ms_per_step": round(host_issue_ms, 3),
+                       "forward_span_ms_median": round(span_ms[len(span_ms) // 2], 3),
+                       "gap_between_forwards_ms_median": round(gap_ms[len(gap_ms) // 2], 3),
                        "bytes_sent_per_rank_per_step": sh.comm_bytes_per_step(),
                        "nvlink_gbs_per_rank": round(sh.comm_bytes_per_step() / (ms.item() * 1e-3) / 1e9, 1)})
         res = {"ms_per_step": ms.item(), "rows_per_rank": hi - lo,

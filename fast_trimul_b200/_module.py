@@ -48,14 +48,23 @@ class DeviceErrorWord:
         self.dev = torch.zeros(64, dtype=torch.int32, device=device)
         self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.event = None
+        self.side = None
         self.ptr = self.dev.data_ptr()
 
     def after_launch(self):
         if torch.cuda.is_current_stream_capturing() or _NO_ASYNC_CHECK:
             return
-        self.host.copy_(self.dev[:1], non_blocking=True)
-        self.event = torch.cuda.Event()
-        self.event.record()
+        # the copy runs on a side stream that waits for this point of the calling stream,
+        # so a busy copy engine can never hold up the work queued after the call
+        if self.side is None:
+            self.side = torch.cuda.Stream(self.device)
+        done = torch.cuda.Event()
+        done.record()
+        self.side.wait_event(done)
+        with torch.cuda.stream(self.side):
+            self.host.copy_(self.dev[:1], non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(self.side)
 
     def _raise(self, code):
         self.dev.zero_()

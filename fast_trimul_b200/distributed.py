@@ -977,6 +977,9 @@ def bench_sharded(args, torch_mod):
     if rank == 0:
         detail.update({"host_issue_ms_per_step": round(host_issue_ms, 3),
                        "forward_span_ms_median": round(span_ms[len(span_ms) // 2], 3),
+                       "forward_span_ms": {"min": round(span_ms[0], 3), "mean": round(sum(span_ms) / K, 3),
+                                           "max": round(span_ms[-1], 3),
+                                           "in_order": [round(a.elapsed_time(b), 3) for a, b in spans]},
                        "gap_between_forwards_ms_median": round(gap_ms[len(gap_ms) // 2], 3),
                        "bytes_sent_per_rank_per_step": sh.comm_bytes_per_step(),
                        "nvlink_gbs_per_rank": round(sh.comm_bytes_per_step() / (ms.item() * 1e-3) / 1e9, 1)})

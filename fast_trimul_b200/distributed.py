@@ -902,15 +902,18 @@ def bench_sharded(args, torch_mod):
     K = args.steps
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     from bench import ClockSampler
-    dist.barrier()
-    torch.cuda.synchronize()
     n_launch0 = _lib.stats["kernel_launches"]
     import time
     if getattr(args, "trace_timed", False) and hasattr(sh, "enable_trace"):
         sh.enable_trace()
     spans = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(K)]
+    # the clock sampler starts (NVML set-up takes milliseconds) before the barrier, so
+    # every rank enters the timed loop at the same moment: otherwise the first forward of
+    # the fastest rank waits for the others' late start inside the timed region
     with ClockSampler(local) as clk:
+        dist.barrier()
+        torch.cuda.synchronize()
         t0.record()
         h0 = time.perf_counter()
         for k in range(K):

@@ -112,12 +112,12 @@ SIGNATURES = {
     "ftm_bwd_ln_in": (ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, ctypes.c_float, _vp, _vp,
                                      ctypes.c_int64, _vp]),
     "ftm_bwd_x_ln": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _i32, _i32, _vp]),
-    "ftm_bwd_gate": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, ctypes.c_float, _vp, _vp, _vp,
+    "ftm_bwd_gate": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp,
                                     _vp, ctypes.c_int64, _vp]),
     "ftm_bwd_x_ln_bwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
-    "ftm_bwd_gates_in": (ctypes.c_int, [_vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _i32, _i32,
+    "ftm_bwd_gates_in": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                         _vp]),
-    "ftm_bwd_ln_in_bwd": (ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.c_float,
+    "ftm_bwd_ln_in_bwd": (ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp,
                                          _i32, _vp, _i32, _vp, ctypes.c_int64, _vp]),
     "ftm_static_scratch_error_word": (_vp, []),
 }

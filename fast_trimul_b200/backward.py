@@ -135,20 +135,17 @@ def native_plane_grads_pos(dx_plane, a16, b16, mode):
     """Gradients of the contraction's operands as fp16 planes in position order.
 
     dx_plane: (L, N, N) fp32 dX[l][i][j]; a16, b16: (L, N, N) fp16 planes of the forward.
-    Returns (dA, dB, scale): dA[l][u][v] * scale is the gradient of a at position (u, v)
-    of channel l (likewise dB) in both modes -- incoming mode's transposed planes are
-    undone by choosing the operand order (dA^T = B^T dX^T is computed directly), so no
-    transpose pass is needed."""
+    Returns (dA, dB, scale) with scale a one-element device tensor: dA[l][u][v] * scale is
+    the gradient of a at position (u, v) of channel l (likewise dB) in both modes --
+    incoming mode's transposed planes are undone by choosing the operand order
+    (dA^T = B^T dX^T is computed directly), so no transpose pass is needed. The scale
+    stays on the device: no host synchronisation."""
     lib = _lib.load()
     L, N, _ = dx_plane.shape
-    scale = dx_plane.abs().amax()
-    sc = float(scale.item())
+    # max |dX|, kept away from zero so an all-zero gradient gives zeros, not NaNs
+    scale = dx_plane.abs().amax().clamp_min(1e-30).reshape(1)
     dA = torch.empty(L, N, N, dtype=torch.float16, device=dx_plane.device)
     dB = torch.empty_like(dA)
-    if sc == 0.0:
-        dA.zero_()
-        dB.zero_()
-        return dA, dB, 0.0
     dx16 = (dx_plane / scale).to(torch.float16)
     err = _lib_err(dx_plane.device)
     s = torch.cuda.current_stream(dx_plane.device).cuda_stream
@@ -166,7 +163,7 @@ def native_plane_grads_pos(dx_plane, a16, b16, mode):
         d.x, d.x_l_stride, d.x_row_stride = out.data_ptr(), N * N, N
         _lib.check(lib.ftm_contraction_general(ctypes.byref(d), err, s), "ftm_contraction_general")
         _lib.stats["kernel_launches"] += 1
-    return dA, dB, sc
+    return dA, dB, scale
 
 
 def backward_native(mod, z, mask, params, planes, grad_out):
@@ -196,10 +193,9 @@ def backward_native(mod, z, mask, params, planes, grad_out):
     gout = grad_out.contiguous()
     if gout.dtype not in _DT:
         gout = gout.float()
-    gmax = float(gout.abs().amax().item())
-    if gmax == 0.0:
-        return torch.zeros_like(z), [torch.zeros_like(t) for t in params]
-    gsc = 1.0 / gmax
+    # largest |dout| as a device scalar (no host synchronisation), kept away from zero
+    gmax = gout.abs().amax().float().clamp_min(1e-30).reshape(1)
+    gsc = (1.0 / gmax).contiguous()
     chk = _lib.check
 
     zn = torch.empty(P, C, dtype=torch.float16, device=dev)
@@ -217,7 +213,7 @@ def backward_native(mod, z, mask, params, planes, grad_out):
     nb = lib.ftm_bwd_partial_blocks()
     part_g = torch.empty(nb, 2 * C, dtype=torch.float32, device=dev)
     chk(lib.ftm_bwd_gate(O.data_ptr(), b_o.data_ptr(), H.data_ptr(), b_g.data_ptr(), gout.data_ptr(),
-                         _DT[gout.dtype], gsc, mp, dO.data_ptr(), dPGZ.data_ptr(), part_g.data_ptr(),
+                         _DT[gout.dtype], gsc.data_ptr(), mp, dO.data_ptr(), dPGZ.data_ptr(), part_g.data_ptr(),
                          P, s), "ftm_bwd_gate")
     del O
     dxn = dO @ W_o
@@ -234,7 +230,7 @@ def backward_native(mod, z, mask, params, planes, grad_out):
     dA, dB, dsc = native_plane_grads_pos(dxp, a16.reshape(L, N, N), b16.reshape(L, N, N), mod.mode)
     del dxp
     part_in = torch.empty(nb, 4 * C, dtype=torch.float32, device=dev)
-    chk(lib.ftm_bwd_gates_in(dA.data_ptr(), dB.data_ptr(), dsc, H.data_ptr(), b_in.data_ptr(),
+    chk(lib.ftm_bwd_gates_in(dA.data_ptr(), dB.data_ptr(), dsc.data_ptr(), H.data_ptr(), b_in.data_ptr(),
                              dPGZ.data_ptr(), part_in.data_ptr(), B, N, s), "ftm_bwd_gates_in")
     del dA, dB, H
     dzn = dPGZ @ W_all                                          # (P, 128)
@@ -244,7 +240,7 @@ def backward_native(mod, z, mask, params, planes, grad_out):
     dz = torch.empty(z.shape, dtype=zc.dtype, device=dev)
     part2 = torch.empty(nb, 2 * C, dtype=torch.float32, device=dev)
     chk(lib.ftm_bwd_ln_in_bwd(zc.data_ptr(), _DT[zc.dtype], mp, zst.data_ptr(), dzn.data_ptr(),
-                              g_in.data_ptr(), gout.data_ptr(), _DT[gout.dtype], gsc,
+                              g_in.data_ptr(), gout.data_ptr(), _DT[gout.dtype], gsc.data_ptr(),
                               1 if mod.residual else 0, dz.data_ptr(), _DT[dz.dtype],
                               part2.data_ptr(), P, s), "ftm_bwd_ln_in_bwd")
     pg2 = part2.sum(0)

@@ -177,7 +177,8 @@ __global__ void x_ln_kernel(const __half* __restrict__ xplane, const float* __re
 // O, H hold the GEMM results without biases.
 __global__ void gate_bwd_kernel(const __half* __restrict__ O, const float* __restrict__ b_o,
                                 const __half* __restrict__ H, const float* __restrict__ b_g,
-                                const void* __restrict__ gout, int g_dtype, float g_scale,
+                                const void* __restrict__ gout, int g_dtype,
+                                const float* __restrict__ g_scale_p,
                                 const float* __restrict__ mask, __half* __restrict__ dO,
                                 __half* __restrict__ dPGZ, float* __restrict__ partial, long long P) {
   __shared__ float red[8][2 * kC];
@@ -193,7 +194,7 @@ __global__ void gate_bwd_kernel(const __half* __restrict__ O, const float* __res
     load4(O, FTM_F16, static_cast<size_t>(p) * kC + 4 * lane, o);
     load4(H, FTM_F16, static_cast<size_t>(p) * kH + 512 + 4 * lane, gz);
     load4(gout, g_dtype, static_cast<size_t>(p) * kC + 4 * lane, g);
-    const float m = (mask ? mask[p] : 1.f) * g_scale;
+    const float m = (mask ? mask[p] : 1.f) * *g_scale_p;
     float dov[4], dgz[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -277,7 +278,7 @@ __global__ void x_ln_bwd_kernel(const __half* __restrict__ xplane, const float2*
 // a = p_a sigmoid(g_a) (same for b): dp = da sigmoid(g), dg = da p sigmoid(g)(1 - sigmoid(g)).
 // da, db come as fp16 planes in position order [b][c][u][v], scaled by `dscale`.
 __global__ void gates_in_bwd_kernel(const __half* __restrict__ dA, const __half* __restrict__ dB,
-                                    float dscale, const __half* __restrict__ H,
+                                    const float* __restrict__ dscale_p, const __half* __restrict__ H,
                                     const float* __restrict__ b_in, __half* __restrict__ dPGZ,
                                     float* __restrict__ partial, int B, int N) {
   __shared__ float ta[kC][kTile + 1];
@@ -310,7 +311,7 @@ __global__ void gates_in_bwd_kernel(const __half* __restrict__ dA, const __half*
         load4(H, FTM_F16, p * kH + half * 256 + 128 + 4 * lane, gr);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float d = (half ? tb : ta)[4 * lane + k][j] * dscale;
+          const float d = (half ? tb : ta)[4 * lane + k][j] * *dscale_p;
           const float pv = pr[k] + bias[2 * half][k];
           const float s = sigmoidf(gr[k] + bias[2 * half + 1][k]);
           dpv[k] = d * s;
@@ -335,8 +336,8 @@ __global__ void gates_in_bwd_kernel(const __half* __restrict__ dA, const __half*
 __global__ void ln_in_bwd_kernel(const void* __restrict__ z, int z_dtype,
                                  const float* __restrict__ mask, const float2* __restrict__ stats,
                                  const __half* __restrict__ dzn, const float* __restrict__ gamma,
-                                 const void* __restrict__ gout, int g_dtype, float g_scale,
-                                 int residual, void* __restrict__ dz, int dz_dtype,
+                                 const void* __restrict__ gout, int g_dtype,
+                                 const float* __restrict__ g_scale_p, int residual, void* __restrict__ dz, int dz_dtype,
                                  float* __restrict__ partial, long long P) {
   __shared__ float red[8][2 * kC];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -367,7 +368,7 @@ __global__ void ln_in_bwd_kernel(const void* __restrict__ z, int z_dtype,
     if (residual) load4(gout, g_dtype, static_cast<size_t>(p) * kC + 4 * lane, res);
     float o[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = (st.y * (gy[k] - s1 - xh[k] * s2) + res[k] * m * g_scale) * m;
+    for (int k = 0; k < 4; ++k) o[k] = (st.y * (gy[k] - s1 - xh[k] * s2) + res[k] * m * *g_scale_p) * m;
     store4(dz, dz_dtype, static_cast<size_t>(p) * kC + 4 * lane, o);
   }
 #pragma unroll
@@ -426,9 +427,9 @@ int ftm_bwd_x_ln(const void* xplane, const float* gamma, const float* beta, floa
 }
 
 int ftm_bwd_gate(const void* O, const float* b_o, const void* H, const float* b_g, const void* gout,
-                 int32_t g_dtype, float g_scale, const float* mask, void* dO, void* dPGZ,
+                 int32_t g_dtype, const float* g_scale, const float* mask, void* dO, void* dPGZ,
                  float* partial, int64_t positions, ftm_stream_t stream) {
-  if (!O || !b_o || !H || !b_g || !gout || !dO || !dPGZ || !partial || positions < 1 ||
+  if (!O || !b_o || !H || !b_g || !gout || !g_scale || !dO || !dPGZ || !partial || positions < 1 ||
       !dtype_ok(g_dtype))
     return FTM_BAD_ARGUMENT;
   gate_bwd_kernel<<<bwd_blocks(), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
@@ -447,9 +448,9 @@ int ftm_bwd_x_ln_bwd(const void* xplane, const float* stats, const void* dxn, co
   return launched(cudaSuccess);
 }
 
-int ftm_bwd_gates_in(const void* dA, const void* dB, float dscale, const void* H, const float* b_in,
+int ftm_bwd_gates_in(const void* dA, const void* dB, const float* dscale, const void* H, const float* b_in,
                      void* dPGZ, float* partial, int32_t batch, int32_t n, ftm_stream_t stream) {
-  if (!dA || !dB || !H || !b_in || !dPGZ || !partial || batch < 1 || n < 1) return FTM_BAD_ARGUMENT;
+  if (!dA || !dB || !dscale || !H || !b_in || !dPGZ || !partial || batch < 1 || n < 1) return FTM_BAD_ARGUMENT;
   gates_in_bwd_kernel<<<bwd_blocks(), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(dA), static_cast<const __half*>(dB), dscale,
       static_cast<const __half*>(H), b_in, static_cast<__half*>(dPGZ), partial, batch, n);
@@ -458,9 +459,9 @@ int ftm_bwd_gates_in(const void* dA, const void* dB, float dscale, const void* H
 
 int ftm_bwd_ln_in_bwd(const void* z, int32_t z_dtype, const float* mask, const float* stats,
                       const void* dzn, const float* gamma, const void* gout, int32_t g_dtype,
-                      float g_scale, int32_t residual, void* dz, int32_t dz_dtype, float* partial,
+                      const float* g_scale, int32_t residual, void* dz, int32_t dz_dtype, float* partial,
                       int64_t positions, ftm_stream_t stream) {
-  if (!z || !stats || !dzn || !gamma || !gout || !dz || !partial || positions < 1 ||
+  if (!z || !stats || !dzn || !gamma || !gout || !g_scale || !dz || !partial || positions < 1 ||
       !dtype_ok(z_dtype) || !dtype_ok(g_dtype) || !dtype_ok(dz_dtype))
     return FTM_BAD_ARGUMENT;
   ln_in_bwd_kernel<<<bwd_blocks(), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(

@@ -221,7 +221,9 @@ int ftm_contraction_scatter(const void* A, const void* B, const ftm_peer_planes*
  * (GEMM results without biases / their gradients). Grids are fixed: partial-sum buffers
  * have ftm_bwd_partial_blocks() rows (256 floats: dgamma then dbeta per channel, or the
  * column sums of the gradient rows a kernel writes -- the bias gradients).
- * g_scale multiplies the output gradient (the caller pre-scales it to unit magnitude). */
+ * g_scale / dscale point to one device float: the factor applied to the output gradient
+ * (the caller pre-scales it to unit magnitude) / to the da, db planes; passing them in
+ * device memory lets the caller compute them without a host synchronisation. */
 int ftm_bwd_partial_blocks(void);
 /* zn = LayerNorm(z * mask) (fp16 rows), stats = (mean, rstd) per position */
 int ftm_bwd_ln_in(const void* z, int32_t z_dtype, const float* mask, const float* gamma,
@@ -233,19 +235,19 @@ int ftm_bwd_x_ln(const void* xplane, const float* gamma, const float* beta, floa
 /* output gate: dO = dout*m*sigmoid(gz), dPGZ[:, 512:640] = dout*m*o*sigmoid'(gz);
  * partial rows of 256: column sums of dO then of dgz */
 int ftm_bwd_gate(const void* O, const float* b_o, const void* H, const float* b_g, const void* gout,
-                 int32_t g_dtype, float g_scale, const float* mask, void* dO, void* dPGZ,
+                 int32_t g_dtype, const float* g_scale, const float* mask, void* dO, void* dPGZ,
                  float* partial, int64_t positions, ftm_stream_t stream);
 /* output LayerNorm backward: dx (fp32 plane) from dxn rows, partial dgamma / dbeta */
 int ftm_bwd_x_ln_bwd(const void* xplane, const float* stats, const void* dxn, const float* gamma,
                      float* dxplane, float* partial, int32_t batch, int32_t n, ftm_stream_t stream);
 /* input gates: dPGZ[:, 0:512] from da, db (fp16 planes in position order, x dscale);
  * partial rows of 512: column sums of dPGZ[:, 0:512] */
-int ftm_bwd_gates_in(const void* dA, const void* dB, float dscale, const void* H, const float* b_in,
+int ftm_bwd_gates_in(const void* dA, const void* dB, const float* dscale, const void* H, const float* b_in,
                      void* dPGZ, float* partial, int32_t batch, int32_t n, ftm_stream_t stream);
 /* input LayerNorm backward (+ the residual path): dz, partial dgamma / dbeta */
 int ftm_bwd_ln_in_bwd(const void* z, int32_t z_dtype, const float* mask, const float* stats,
                       const void* dzn, const float* gamma, const void* gout, int32_t g_dtype,
-                      float g_scale, int32_t residual, void* dz, int32_t dz_dtype, float* partial,
+                      const float* g_scale, int32_t residual, void* dz, int32_t dz_dtype, float* partial,
                       int64_t positions, ftm_stream_t stream);
 
 /* ---- row-sharded multi-GPU forward, native exchange pipeline ----------------
